@@ -1,0 +1,406 @@
+// fmoe_api.cu -- host side of the C ABI declared in include/fmoe.h.
+//
+// Restates the reference's host orchestration (solution/cuda/kernel.cu:1727-1837 and
+// the two pipelines at :1447-1720) for the B200 kernels:
+//   * argument checks mirror CheckTensor / CheckSameDevice (kernel.cu:121-168) for
+//     what a pointer ABI can check (sizes, geometry, alignment);
+//   * no per-call allocation, no host round trip and no stream synchronisation: the
+//     reference's cudaStreamSynchronize (kernel.cu:1544, :1834), pinned-host count copy
+//     and per-call cudaMallocAsync (kernel.cu:1532-1546, :1290-1310) are replaced by
+//     device-side planning in route_plan_kernel and a caller-owned workspace;
+//   * one pipeline for every T; the token tile comes from the autotune table instead of
+//     the reference's fixed T <= 512 switch (kernel.cu:47, :1781).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <climits>
+#include <cstdio>
+#include <mutex>
+#include <string>
+
+#include "../../include/fmoe.h"
+#include "autotune_table.h"
+#include "fmoe_common.cuh"
+#include "fmoe_kernels.cuh"
+
+namespace fmoe {
+namespace {
+
+thread_local std::string g_last_error;
+thread_local cudaEvent_t g_stage_events[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
+thread_local bool g_stage_on = false;
+
+int mark_stage(int i, cudaStream_t s);
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+#define FMOE_CUDA_TRY(expr)                                                              \
+  do {                                                                                   \
+    cudaError_t err__ = (expr);                                                          \
+    if (err__ != cudaSuccess)                                                            \
+      return fail(FMOE_ERR_RUNTIME, std::string("CUDA error at ") + __FILE__ + ":" +      \
+                                        std::to_string(__LINE__) + ": " +                \
+                                        cudaGetErrorString(err__));                      \
+  } while (0)
+
+Geometry to_geometry(const fmoe_problem& p) {
+  Geometry g;
+  g.T = p.num_tokens;
+  g.E = p.num_experts;
+  g.E_local = p.num_local_experts;
+  g.H = p.hidden_size;
+  g.I = p.intermediate_size;
+  g.top_k = p.top_k;
+  g.n_group = p.n_group;
+  g.topk_group = p.topk_group;
+  return g;
+}
+
+int validate(const fmoe_problem* p) {
+  if (!p) return fail(FMOE_ERR_VALUE, "problem must not be NULL");
+  if (p->num_tokens < 0) return fail(FMOE_ERR_VALUE, "num_tokens must be >= 0");
+  if (p->num_tokens > (int64_t)1 << 24)
+    return fail(FMOE_ERR_VALUE, "num_tokens exceeds 2^24");
+  if (p->num_experts < 1 || p->num_experts > 256)
+    return fail(FMOE_ERR_VALUE, "num_experts must be in [1, 256]");
+  if (p->n_group < 1 || p->n_group > 32 || p->num_experts % p->n_group != 0)
+    return fail(FMOE_ERR_VALUE, "n_group must be in [1, 32] and divide num_experts");
+  if (p->topk_group < 1 || p->topk_group > p->n_group)
+    return fail(FMOE_ERR_VALUE, "topk_group must be in [1, n_group]");
+  if (p->top_k < 1 || p->top_k > 32 ||
+      p->top_k > p->topk_group * (p->num_experts / p->n_group))
+    return fail(FMOE_ERR_VALUE, "top_k must be in [1, 32] and fit in the kept groups");
+  if (p->num_local_experts < 1 || p->num_local_experts > 64)
+    return fail(FMOE_ERR_VALUE, "num_local_experts must be in [1, 64]");
+  if (p->hidden_size < 128 || p->hidden_size % 128 != 0 || p->hidden_size > 65536)
+    return fail(FMOE_ERR_VALUE, "hidden_size must be a positive multiple of 128 (<= 65536)");
+  if (p->intermediate_size < 128 || p->intermediate_size % 128 != 0 ||
+      p->intermediate_size > 65536)
+    return fail(FMOE_ERR_VALUE,
+                "intermediate_size must be a positive multiple of 128 (<= 65536)");
+  if (p->tile_n != 0 && !gemm_bn_supported(p->tile_n))
+    return fail(FMOE_ERR_VALUE, "tile_n must be 0 or one of 16, 32, 64, 128, 256");
+  const WorkspaceLayout L = make_layout(to_geometry(*p));
+  if (L.row_cap * (int64_t)p->hidden_size >= ((int64_t)1 << 40))
+    return fail(FMOE_ERR_VALUE, "problem too large for the row-permuted workspace");
+  return FMOE_OK;
+}
+
+bool aligned(const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; }
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
+                                         cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  });
+  return fn;
+}
+
+// 2D byte tensor [outer, inner] with row pitch `pitch` bytes; box [box_outer, box_inner].
+int make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch,
+             uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz, const char* what) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(FMOE_ERR_RUNTIME, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {pitch};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(FMOE_ERR_RUNTIME, std::string("tensor map encode failed for ") + what +
+                                      " (CUresult " + std::to_string((int)r) + ")");
+  return FMOE_OK;
+}
+
+int num_sms_current() {
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+int mark_stage(int i, cudaStream_t s) {
+  if (!g_stage_on) return FMOE_OK;
+  FMOE_CUDA_TRY(cudaEventRecord(g_stage_events[i], s));
+  return FMOE_OK;
+}
+
+struct Carved {
+  WorkspaceLayout L;
+  uint8_t* base;
+  template <typename T>
+  T* at(size_t off) const {
+    return reinterpret_cast<T*>(base + off);
+  }
+};
+
+int carve(const fmoe_problem* p, void* ws, size_t ws_bytes, Carved* c) {
+  c->L = make_layout(to_geometry(*p));
+  if (!ws) return fail(FMOE_ERR_WORKSPACE, "workspace must not be NULL");
+  if (!aligned(ws, 256)) return fail(FMOE_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+  if (ws_bytes < c->L.total)
+    return fail(FMOE_ERR_WORKSPACE, "workspace too small: need " + std::to_string(c->L.total) +
+                                        " bytes, got " + std::to_string(ws_bytes));
+  c->base = static_cast<uint8_t*>(ws);
+  return FMOE_OK;
+}
+
+RouteArgs route_args(const fmoe_problem* p, const Carved& c, const float* logits,
+                     const void* bias, int bn) {
+  RouteArgs a;
+  a.logits = logits;
+  a.bias = static_cast<const uint16_t*>(bias);
+  a.T = p->num_tokens;
+  a.E = p->num_experts;
+  a.n_group = p->n_group;
+  a.topk_group = p->topk_group;
+  a.top_k = p->top_k;
+  a.E_local = p->num_local_experts;
+  a.local_offset = p->local_expert_offset;
+  a.rsf = p->routed_scaling_factor;
+  a.bn = bn;
+  a.row_cap = c.L.row_cap;
+  a.max_chunks = c.L.max_chunks;
+  a.topk_idx = c.at<int>(c.L.topk_idx);
+  a.topk_w = c.at<float>(c.L.topk_w);
+  a.cta_counts = c.at<int>(c.L.cta_counts);
+  a.cta_base = c.at<int>(c.L.cta_base);
+  a.expert_cnt = c.at<int>(c.L.expert_cnt);
+  a.expert_off = c.at<int>(c.L.expert_off);
+  a.meta = c.at<int>(c.L.meta);
+  a.chunks = c.at<Chunk>(c.L.chunks);
+  return a;
+}
+
+int launch_route(const fmoe_problem* p, const Carved& c, const float* logits, const void* bias,
+                 int bn, cudaStream_t stream) {
+  FMOE_CUDA_TRY(cudaMemsetAsync(c.at<int>(c.L.meta), 0, kMetaWords * sizeof(int), stream));
+  const RouteArgs ra = route_args(p, c, logits, bias, bn);
+  route_plan_kernel<<<(unsigned)c.L.n_route_ctas, kRouteTokensPerCta * 32, 0, stream>>>(ra);
+  FMOE_CUDA_TRY(cudaGetLastError());
+  return FMOE_OK;
+}
+
+}  // namespace
+}  // namespace fmoe
+
+using namespace fmoe;
+
+extern "C" int fmoe_abi_version(void) { return FMOE_ABI_VERSION; }
+
+extern "C" const char* fmoe_last_error(void) { return g_last_error.c_str(); }
+
+extern "C" int fmoe_validate(const fmoe_problem* p) { return validate(p); }
+
+extern "C" int fmoe_autotune_tile_n(int64_t num_tokens) { return autotune_tile_n(num_tokens); }
+
+extern "C" int fmoe_workspace_size(const fmoe_problem* p, size_t* bytes) {
+  const int v = validate(p);
+  if (v != FMOE_OK) return v;
+  if (!bytes) return fail(FMOE_ERR_VALUE, "bytes must not be NULL");
+  *bytes = make_layout(to_geometry(*p)).total;
+  return FMOE_OK;
+}
+
+extern "C" int fmoe_forward(const fmoe_problem* p, const fmoe_tensors* t, void* workspace,
+                            size_t workspace_bytes, void* stream_ptr) {
+  int v = validate(p);
+  if (v != FMOE_OK) return v;
+  if (!t) return fail(FMOE_ERR_VALUE, "tensors must not be NULL");
+  if (p->num_tokens == 0) return FMOE_OK;  // empty batch: nothing to write
+  const void* ptrs[] = {t->routing_logits, t->routing_bias, t->hidden_states,
+                        t->hidden_states_scale, t->gemm1_weights, t->gemm1_weights_scale,
+                        t->gemm2_weights, t->gemm2_weights_scale, t->output};
+  const char* names[] = {"routing_logits", "routing_bias", "hidden_states",
+                         "hidden_states_scale", "gemm1_weights", "gemm1_weights_scale",
+                         "gemm2_weights", "gemm2_weights_scale", "output"};
+  for (int i = 0; i < 9; ++i) {
+    if (!ptrs[i]) return fail(FMOE_ERR_VALUE, std::string(names[i]) + " must not be NULL");
+    if (!aligned(ptrs[i], 16))
+      return fail(FMOE_ERR_VALUE, std::string(names[i]) + " must be 16-byte aligned");
+  }
+  Carved c;
+  v = carve(p, workspace, workspace_bytes, &c);
+  if (v != FMOE_OK) return v;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const int bn = p->tile_n ? p->tile_n : autotune_tile_n(p->num_tokens);
+  const int64_t T = p->num_tokens;
+  const int H = p->hidden_size, I = p->intermediate_size, EL = p->num_local_experts;
+
+  if ((v = mark_stage(0, stream)) != FMOE_OK) return v;
+  v = launch_route(p, c, t->routing_logits, t->routing_bias, bn, stream);
+  if (v != FMOE_OK) return v;
+  if ((v = mark_stage(1, stream)) != FMOE_OK) return v;
+
+  ScatterArgs sa;
+  sa.hidden = static_cast<const uint8_t*>(t->hidden_states);
+  sa.hidden_scale = t->hidden_states_scale;
+  sa.T = T;
+  sa.H = H;
+  sa.top_k = p->top_k;
+  sa.E_local = EL;
+  sa.local_offset = p->local_expert_offset;
+  sa.row_cap = c.L.row_cap;
+  sa.topk_idx = c.at<int>(c.L.topk_idx);
+  sa.topk_w = c.at<float>(c.L.topk_w);
+  sa.cta_base = c.at<int>(c.L.cta_base);
+  sa.expert_cnt = c.at<int>(c.L.expert_cnt);
+  sa.expert_off = c.at<int>(c.L.expert_off);
+  sa.token_row = c.at<int>(c.L.token_row);
+  sa.row_token = c.at<int>(c.L.row_token);
+  sa.row_w = c.at<float>(c.L.row_w);
+  sa.a_perm = c.at<uint8_t>(c.L.a_perm);
+  sa.a_scale = c.at<float>(c.L.a_scale);
+  sa.meta = c.at<int>(c.L.meta);
+  scatter_gather_kernel<<<(unsigned)c.L.n_route_ctas, 256, 0, stream>>>(sa);
+  FMOE_CUDA_TRY(cudaGetLastError());
+  if ((v = mark_stage(2, stream)) != FMOE_OK) return v;
+
+  CUtensorMap m_w13, m_a, m_w2, m_cq;
+  if ((v = make_map(&m_w13, t->gemm1_weights, H, (uint64_t)EL * 2 * I, H, 128, 64,
+                    CU_TENSOR_MAP_SWIZZLE_128B, "gemm1_weights")) != FMOE_OK)
+    return v;
+  if ((v = make_map(&m_a, sa.a_perm, H, c.L.row_cap, H, 128, bn, CU_TENSOR_MAP_SWIZZLE_128B,
+                    "permuted activations")) != FMOE_OK)
+    return v;
+  if ((v = make_map(&m_w2, t->gemm2_weights, I, (uint64_t)EL * H, I, 64, 128,
+                    CU_TENSOR_MAP_SWIZZLE_64B, "gemm2_weights")) != FMOE_OK)
+    return v;
+  uint8_t* cq = c.at<uint8_t>(c.L.cq);
+  if ((v = make_map(&m_cq, cq, 2 * (uint64_t)I, c.L.row_cap, 2 * (uint64_t)I, 128, bn,
+                    CU_TENSOR_MAP_SWIZZLE_128B, "quantised intermediate")) != FMOE_OK)
+    return v;
+
+  GemmArgs g;
+  g.chunks = c.at<Chunk>(c.L.chunks);
+  g.meta = c.at<int>(c.L.meta);
+  g.H = H;
+  g.I = I;
+  g.row_cap = c.L.row_cap;
+  g.cq = cq;
+  g.c_scale = c.at<float>(c.L.c_scale);
+  g.row_w = c.at<float>(c.L.row_w);
+  g.ow = c.at<__nv_bfloat16>(c.L.ow);
+  g.err = c.at<int>(c.L.meta) + kMetaError;
+  const int sms = num_sms_current();
+
+  g.m_tiles = I / 64;
+  g.k_steps = H / kBlock;
+  g.w_scale = t->gemm1_weights_scale;
+  g.act_scale = sa.a_scale;
+  int64_t bound = c.L.max_chunks * (int64_t)g.m_tiles;
+  FMOE_CUDA_TRY(launch_gemm1(bn, m_w13, m_a, g, (int)(bound < sms ? bound : sms), stream));
+  if ((v = mark_stage(3, stream)) != FMOE_OK) return v;
+
+  g.m_tiles = H / kBlock;
+  g.k_steps = I / 64;
+  g.w_scale = t->gemm2_weights_scale;
+  g.act_scale = g.c_scale;
+  bound = c.L.max_chunks * (int64_t)g.m_tiles;
+  FMOE_CUDA_TRY(launch_gemm2(bn, m_w2, m_cq, g, (int)(bound < sms ? bound : sms), stream));
+  if ((v = mark_stage(4, stream)) != FMOE_OK) return v;
+
+  CombineArgs ca;
+  ca.token_row = sa.token_row;
+  ca.ow = g.ow;
+  ca.out = static_cast<__nv_bfloat16*>(t->output);
+  ca.T = T;
+  ca.H = H;
+  ca.top_k = p->top_k;
+  combine_kernel<<<(unsigned)T, 128, 0, stream>>>(ca);
+  FMOE_CUDA_TRY(cudaGetLastError());
+  return mark_stage(5, stream);
+}
+
+extern "C" int fmoe_set_stage_events(void* const* events) {
+  if (!events) {
+    g_stage_on = false;
+    return FMOE_OK;
+  }
+  for (int i = 0; i < 6; ++i) {
+    if (!events[i]) return fail(FMOE_ERR_VALUE, "stage events must not be NULL");
+    g_stage_events[i] = static_cast<cudaEvent_t>(events[i]);
+  }
+  g_stage_on = true;
+  return FMOE_OK;
+}
+
+extern "C" int fmoe_route(const fmoe_problem* p, const float* routing_logits,
+                          const void* routing_bias, const fmoe_route_out* out, void* workspace,
+                          size_t workspace_bytes, void* stream_ptr) {
+  int v = validate(p);
+  if (v != FMOE_OK) return v;
+  if (p->num_tokens == 0) return FMOE_OK;
+  if (!routing_logits || !routing_bias || !out || !out->topk_idx || !out->topk_w)
+    return fail(FMOE_ERR_VALUE, "routing pointers must not be NULL");
+  Carved c;
+  v = carve(p, workspace, workspace_bytes, &c);
+  if (v != FMOE_OK) return v;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const int bn = p->tile_n ? p->tile_n : autotune_tile_n(p->num_tokens);
+  v = launch_route(p, c, routing_logits, routing_bias, bn, stream);
+  if (v != FMOE_OK) return v;
+  const size_t n = (size_t)p->num_tokens * p->top_k;
+  FMOE_CUDA_TRY(cudaMemcpyAsync(out->topk_idx, c.at<int>(c.L.topk_idx), n * 4,
+                                cudaMemcpyDeviceToDevice, stream));
+  FMOE_CUDA_TRY(cudaMemcpyAsync(out->topk_w, c.at<float>(c.L.topk_w), n * 4,
+                                cudaMemcpyDeviceToDevice, stream));
+  return FMOE_OK;
+}
+
+extern "C" int fmoe_read_device_error(const fmoe_problem* p, void* workspace, void* stream_ptr,
+                                      int32_t* device_error) {
+  int v = validate(p);
+  if (v != FMOE_OK) return v;
+  if (!workspace || !device_error) return fail(FMOE_ERR_VALUE, "NULL argument");
+  const WorkspaceLayout L = make_layout(to_geometry(*p));
+  int* word = reinterpret_cast<int*>(static_cast<uint8_t*>(workspace) + L.meta) + kMetaError;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  FMOE_CUDA_TRY(cudaStreamSynchronize(stream));
+  int host = 0;
+  FMOE_CUDA_TRY(cudaMemcpy(&host, word, sizeof(int), cudaMemcpyDeviceToHost));
+  FMOE_CUDA_TRY(cudaMemset(word, 0, sizeof(int)));
+  *device_error = host;
+  if (host != 0) {
+    char buf[96];
+    std::snprintf(buf, sizeof(buf), "device error word 0x%x", host);
+    g_last_error = buf;
+  }
+  return FMOE_OK;
+}
+
+extern "C" int fmoe_plan_view_get(const fmoe_problem* p, void* workspace, fmoe_plan_view* view) {
+  int v = validate(p);
+  if (v != FMOE_OK) return v;
+  if (!workspace || !view) return fail(FMOE_ERR_VALUE, "NULL argument");
+  const WorkspaceLayout L = make_layout(to_geometry(*p));
+  uint8_t* b = static_cast<uint8_t*>(workspace);
+  view->expert_cnt = reinterpret_cast<const int32_t*>(b + L.expert_cnt);
+  view->expert_off = reinterpret_cast<const int32_t*>(b + L.expert_off);
+  view->row_token = reinterpret_cast<const int32_t*>(b + L.row_token);
+  view->token_row = reinterpret_cast<const int32_t*>(b + L.token_row);
+  view->meta = reinterpret_cast<const int32_t*>(b + L.meta);
+  view->row_cap = L.row_cap;
+  return FMOE_OK;
+}

@@ -1,0 +1,86 @@
+// fmoe_kernels.cuh -- argument blocks and launch entry points of the fused MoE kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include "fmoe_common.cuh"
+
+namespace fmoe {
+
+struct RouteArgs {
+  const float* logits;     // [T, E]
+  const uint16_t* bias;    // [E] bf16 bits
+  int64_t T;
+  int E, n_group, topk_group, top_k, E_local, local_offset;
+  float rsf;
+  int bn;                  // token tile of the grouped GEMMs (chunk size)
+  int64_t row_cap, max_chunks;
+  int* topk_idx;           // [T, K]
+  float* topk_w;           // [T, K]
+  int* cta_counts;         // [n_ctas, E_local]
+  int* cta_base;           // [n_ctas, E_local]
+  int* expert_cnt;         // [E_local]
+  int* expert_off;         // [E_local + 1]
+  int* meta;               // [kMetaWords]
+  Chunk* chunks;           // [max_chunks]
+};
+
+struct ScatterArgs {
+  const uint8_t* hidden;        // [T, H] e4m3
+  const float* hidden_scale;    // [H/128, T]
+  int64_t T;
+  int H, top_k, E_local, local_offset;
+  int64_t row_cap;
+  const int* topk_idx;
+  const float* topk_w;
+  const int* cta_base;
+  const int* expert_cnt;
+  const int* expert_off;
+  int* token_row;               // [T, K]
+  int* row_token;               // [row_cap]
+  float* row_w;                 // [row_cap]
+  uint8_t* a_perm;              // [row_cap, H]
+  float* a_scale;               // [H/128, row_cap]
+  int* meta;
+};
+
+struct GemmArgs {
+  const Chunk* chunks;
+  const int* meta;
+  int m_tiles;             // weight-row tiles per expert (I/64 for GEMM1, H/128 for GEMM2)
+  int k_steps;             // H/128 (GEMM1) or I/64 (GEMM2)
+  int H, I;
+  int64_t row_cap;         // leading dimension of the activation scale arrays
+  const float* w_scale;    // [E_local, rows/128, cols/128]
+  const float* act_scale;  // GEMM1: a_scale [H/128, row_cap]; GEMM2: c_scale [I/64, row_cap]
+  // GEMM1 outputs
+  uint8_t* cq;             // [row_cap, 2I]: per 64-column block j, 64 hi bytes then 64 lo bytes
+  float* c_scale;          // [I/64, row_cap]
+  // GEMM2 inputs / outputs
+  const float* row_w;      // [row_cap]
+  __nv_bfloat16* ow;       // [row_cap, H] weighted expert outputs
+  int* err;                // device error word
+};
+
+struct CombineArgs {
+  const int* token_row;         // [T, K]
+  const __nv_bfloat16* ow;      // [row_cap, H]
+  __nv_bfloat16* out;           // [T, H]
+  int64_t T;
+  int H, top_k;
+};
+
+__global__ void route_plan_kernel(RouteArgs a);
+__global__ void scatter_gather_kernel(ScatterArgs a);
+__global__ void combine_kernel(CombineArgs a);
+
+// Grouped GEMM launchers (gemm_sm100.cu). `bn` selects the token tile; returns a CUDA error.
+cudaError_t launch_gemm1(int bn, const CUtensorMap& w13_map, const CUtensorMap& a_map,
+                         const GemmArgs& args, int grid, cudaStream_t stream);
+cudaError_t launch_gemm2(int bn, const CUtensorMap& w2_map, const CUtensorMap& cq_map,
+                         const GemmArgs& args, int grid, cudaStream_t stream);
+bool gemm_bn_supported(int bn);
+
+}  // namespace fmoe

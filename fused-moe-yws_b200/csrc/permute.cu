@@ -1,0 +1,155 @@
+// permute.cu -- stable expert-major scatter with fused FP8 row gather, and the final
+// per-token combine.
+//
+// scatter_gather_kernel restates the reference's reorder + gather
+// (solution/cuda/kernel.cu:553-592 and :761-816) with three changes:
+//   * rows are ordered by (local expert, token, k) -- a stable counting sort using the
+//     per-CTA bases from route_plan_kernel -- so the permutation is deterministic;
+//   * the FP8 rows are copied as 16-byte vectors and stay FP8 (the reference
+//     dequantises them to fp32/fp16 in HBM); their per-128-column scales are gathered
+//     into a [H/128, row_cap] array beside them;
+//   * each expert's segment is padded to 16 rows; padding rows are zeroed.
+//
+// combine_kernel restates final_reduce_cast_grouped_kernel (kernel.cu:864-891): each
+// token sums its local routes in top-k order (the routing weight was already applied
+// by the GEMM2 epilogue) and casts to bf16. Tokens with no local route get zeros.
+#include "fmoe_common.cuh"
+#include "fmoe_kernels.cuh"
+
+namespace fmoe {
+
+namespace {
+constexpr int kTok = kRouteTokensPerCta;
+constexpr int kMaxEntries = kTok * 32;
+
+__device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+}  // namespace
+
+__global__ void __launch_bounds__(256) scatter_gather_kernel(ScatterArgs a) {
+  __shared__ int s_le[kMaxEntries];
+  __shared__ int s_row[kMaxEntries];
+  __shared__ int s_list[kMaxEntries];
+  __shared__ int s_base[64];
+  __shared__ int s_nlocal;
+
+  const int tid = threadIdx.x;
+  const int K = a.top_k, nent = kTok * K;
+  const int64_t t0 = (int64_t)blockIdx.x * kTok;
+  for (int e = tid; e < a.E_local; e += blockDim.x)
+    s_base[e] = a.cta_base[(int64_t)blockIdx.x * a.E_local + e];
+  for (int i = tid; i < nent; i += blockDim.x) {
+    const int64_t t = t0 + i / K;
+    int le = -1;
+    if (t < a.T) {
+      const int ge = a.topk_idx[t * K + i % K];
+      const int l = ge - a.local_offset;
+      if (ge >= 0 && l >= 0 && l < a.E_local) le = l;
+    }
+    s_le[i] = le;
+  }
+  __syncthreads();
+  for (int i = tid; i < nent; i += blockDim.x) {
+    const int le = s_le[i];
+    const int64_t t = t0 + i / K;
+    int row = -1;
+    if (le >= 0) {
+      int rank = 0;
+      for (int j = 0; j < i; ++j) rank += s_le[j] == le;
+      row = s_base[le] + rank;
+      if (row >= a.row_cap) {
+        atomicOr(a.meta + kMetaError, kErrRowOverflow);
+        row = -1;
+      }
+    }
+    s_row[i] = row;
+    if (t < a.T) a.token_row[t * K + i % K] = row;
+    if (row >= 0) {
+      a.row_token[row] = (int)t;
+      a.row_w[row] = a.topk_w[t * K + i % K];
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int n = 0;
+    for (int i = 0; i < nent; ++i)
+      if (s_row[i] >= 0) s_list[n++] = i;
+    s_nlocal = n;
+  }
+  __syncthreads();
+  const int n = s_nlocal;
+  const int vpr = a.H / 16;
+  for (int v = tid; v < n * vpr; v += blockDim.x) {
+    const int li = v / vpr, part = v - li * vpr;
+    const int i = s_list[li];
+    const int64_t t = t0 + i / K;
+    const uint4 x = ld_nc_v4(a.hidden + t * a.H + part * 16);
+    *reinterpret_cast<uint4*>(a.a_perm + (int64_t)s_row[i] * a.H + part * 16) = x;
+  }
+  const int kb = a.H / kBlock;
+  for (int v = tid; v < n * kb; v += blockDim.x) {
+    const int li = v / kb, b = v - li * kb;
+    const int i = s_list[li];
+    const int64_t t = t0 + i / K;
+    a.a_scale[(int64_t)b * a.row_cap + s_row[i]] = a.hidden_scale[(int64_t)b * a.T + t];
+  }
+  // padding rows of the experts this CTA owns (expert e goes to CTA e % gridDim.x)
+  for (int e = blockIdx.x; e < a.E_local; e += gridDim.x) {
+    const int cnt = a.expert_cnt[e];
+    const int r0 = a.expert_off[e] + cnt;
+    const int npad = (cnt + kRowAlign - 1) / kRowAlign * kRowAlign - cnt;
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    for (int v = tid; v < npad * vpr; v += blockDim.x) {
+      const int r = r0 + v / vpr;
+      if (r < a.row_cap)
+        *reinterpret_cast<uint4*>(a.a_perm + (int64_t)r * a.H + (v % vpr) * 16) = z;
+    }
+    for (int v = tid; v < npad * kb; v += blockDim.x) {
+      const int r = r0 + v / kb;
+      if (r < a.row_cap) a.a_scale[(int64_t)(v % kb) * a.row_cap + r] = 0.0f;
+    }
+    for (int v = tid; v < npad; v += blockDim.x) {
+      if (r0 + v < a.row_cap) {
+        a.row_token[r0 + v] = -1;
+        a.row_w[r0 + v] = 0.0f;
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(128) combine_kernel(CombineArgs a) {
+  __shared__ int s_rows[32];
+  const int64_t t = blockIdx.x;
+  if (threadIdx.x < a.top_k) s_rows[threadIdx.x] = a.token_row[t * a.top_k + threadIdx.x];
+  __syncthreads();
+  const int nv = a.H / 8;
+  for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+    for (int k = 0; k < a.top_k; ++k) {
+      const int row = s_rows[k];
+      if (row < 0) continue;
+      const uint4 x = ld_nc_v4(a.ow + (int64_t)row * a.H + v * 8);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&x);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(h[j]);
+        acc[2 * j] += f.x;
+        acc[2 * j + 1] += f.y;
+      }
+    }
+    uint4 o;
+    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+    *reinterpret_cast<uint4*>(a.out + t * a.H + v * 8) = o;
+  }
+}
+
+}  // namespace fmoe

@@ -1,0 +1,339 @@
+"""B200-native fused FP8 block-scaled DeepSeek-V3 MoE operator (Python host mirror).
+
+``kernel(...)`` has the argument order, tensor contract and error behaviour of the
+reference operator (YuWei-CH/Fused-MoE-YWS ``solution/cuda/kernel.cu:1727-1837``, and its
+Python global ``flashinfer.kernel`` in ``solution/cuda/binding.py:49-73``):
+
+* ``ValueError`` for a wrong device, layout, rank or shape (``kernel.cu:121-168``);
+* ``TypeError`` for a wrong dtype (``kernel.cu:145-150``);
+* ``RuntimeError`` for CUDA failures (``kernel.cu:53-62``).
+
+All work happens in ``lib/libfmoe.so`` (hand-written sm_100a CUDA behind the C ABI in
+``include/fmoe.h``). There is no fallback: if the library or a CUDA device is missing,
+calls raise ``RuntimeError``.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+from . import workloads  # noqa: F401  (seeded synthetic inputs)
+from .workloads import ROUTING_BY_EXPERTS
+
+_PKG_ROOT = Path(__file__).resolve().parent.parent
+LIB_PATH = _PKG_ROOT / "lib" / "libfmoe.so"
+TVM_FFI_LIB_PATH = _PKG_ROOT / "lib" / "libfmoe_tvm_ffi.so"
+
+FMOE_OK, FMOE_ERR_VALUE, FMOE_ERR_TYPE, FMOE_ERR_RUNTIME, FMOE_ERR_WORKSPACE, FMOE_ERR_DEVICE = range(6)
+
+EXPORTED_SYMBOLS = ("fmoe_abi_version", "fmoe_last_error", "fmoe_validate", "fmoe_workspace_size",
+                    "fmoe_autotune_tile_n", "fmoe_forward", "fmoe_route", "fmoe_read_device_error",
+                    "fmoe_plan_view_get", "fmoe_set_stage_events")
+
+
+class FmoeProblem(ctypes.Structure):
+    _fields_ = [("num_tokens", ctypes.c_int64), ("num_experts", ctypes.c_int32),
+                ("num_local_experts", ctypes.c_int32), ("hidden_size", ctypes.c_int32),
+                ("intermediate_size", ctypes.c_int32), ("top_k", ctypes.c_int32),
+                ("n_group", ctypes.c_int32), ("topk_group", ctypes.c_int32),
+                ("local_expert_offset", ctypes.c_int32), ("routed_scaling_factor", ctypes.c_float),
+                ("tile_n", ctypes.c_int32)]
+
+
+class FmoeTensors(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in (
+        "routing_logits", "routing_bias", "hidden_states", "hidden_states_scale", "gemm1_weights",
+        "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale", "output")]
+
+
+class FmoeRouteOut(ctypes.Structure):
+    _fields_ = [("topk_idx", ctypes.c_void_p), ("topk_w", ctypes.c_void_p)]
+
+
+class FmoePlanView(ctypes.Structure):
+    _fields_ = [("expert_cnt", ctypes.c_void_p), ("expert_off", ctypes.c_void_p),
+                ("row_token", ctypes.c_void_p), ("token_row", ctypes.c_void_p),
+                ("meta", ctypes.c_void_p), ("row_cap", ctypes.c_int64)]
+
+
+_lib = None
+_lib_lock = threading.Lock()
+
+
+def load_library(path: Path | str | None = None):
+    """Load (once) and return the ctypes handle of libfmoe.so; raises if it is missing."""
+    global _lib
+    with _lib_lock:
+        if _lib is not None and path is None:
+            return _lib
+        p = Path(path) if path is not None else LIB_PATH
+        if not p.exists():
+            raise RuntimeError(
+                f"fused MoE library not built: {p} (run `python fused-moe-yws_b200/build.py`)")
+        lib = ctypes.CDLL(str(p))
+        lib.fmoe_abi_version.restype = ctypes.c_int
+        lib.fmoe_last_error.restype = ctypes.c_char_p
+        lib.fmoe_validate.argtypes = [ctypes.POINTER(FmoeProblem)]
+        lib.fmoe_workspace_size.argtypes = [ctypes.POINTER(FmoeProblem),
+                                            ctypes.POINTER(ctypes.c_size_t)]
+        lib.fmoe_autotune_tile_n.argtypes = [ctypes.c_int64]
+        lib.fmoe_forward.argtypes = [ctypes.POINTER(FmoeProblem), ctypes.POINTER(FmoeTensors),
+                                     ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+        lib.fmoe_route.argtypes = [ctypes.POINTER(FmoeProblem), ctypes.c_void_p, ctypes.c_void_p,
+                                   ctypes.POINTER(FmoeRouteOut), ctypes.c_void_p, ctypes.c_size_t,
+                                   ctypes.c_void_p]
+        lib.fmoe_read_device_error.argtypes = [ctypes.POINTER(FmoeProblem), ctypes.c_void_p,
+                                               ctypes.c_void_p, ctypes.POINTER(ctypes.c_int32)]
+        lib.fmoe_plan_view_get.argtypes = [ctypes.POINTER(FmoeProblem), ctypes.c_void_p,
+                                           ctypes.POINTER(FmoePlanView)]
+        lib.fmoe_set_stage_events.argtypes = [ctypes.c_void_p]
+        for name in EXPORTED_SYMBOLS:
+            if not hasattr(lib, name):
+                raise RuntimeError(f"{p} does not export {name}")
+        if path is None:
+            _lib = lib
+        return lib
+
+
+def _raise(lib, rc: int, where: str):
+    msg = lib.fmoe_last_error().decode(errors="replace")
+    text = f"{where}: {msg}"
+    if rc in (FMOE_ERR_VALUE, FMOE_ERR_WORKSPACE):
+        raise ValueError(text)
+    if rc == FMOE_ERR_TYPE:
+        raise TypeError(text)
+    raise RuntimeError(text)
+
+
+def make_problem(T, E, E_local, H, I, local_expert_offset=0, routed_scaling_factor=2.5,
+                 n_group=None, topk_group=None, top_k=None, tile_n=0) -> FmoeProblem:
+    if n_group is None or topk_group is None or top_k is None:
+        if E not in ROUTING_BY_EXPERTS:
+            raise ValueError(f"routing_logits: unsupported number of experts {E}")
+        ng, kg, k = ROUTING_BY_EXPERTS[E]
+        n_group = ng if n_group is None else n_group
+        topk_group = kg if topk_group is None else topk_group
+        top_k = k if top_k is None else top_k
+    return FmoeProblem(int(T), int(E), int(E_local), int(H), int(I), int(top_k), int(n_group),
+                       int(topk_group), int(local_expert_offset), float(routed_scaling_factor),
+                       int(tile_n))
+
+
+def workspace_bytes(prob: FmoeProblem) -> int:
+    lib = load_library()
+    n = ctypes.c_size_t(0)
+    rc = lib.fmoe_workspace_size(ctypes.byref(prob), ctypes.byref(n))
+    if rc != FMOE_OK:
+        _raise(lib, rc, "workspace_size")
+    return int(n.value)
+
+
+class Workspace:
+    """Grow-only device scratch buffer, one per device (the reference keeps thread-local
+    grow-only caches for the same purpose, kernel.cu:234-270)."""
+
+    _per_device: dict = {}
+    _lock = threading.Lock()
+
+    @classmethod
+    def get(cls, device: torch.device, nbytes: int) -> torch.Tensor:
+        key = (device.type, device.index)
+        with cls._lock:
+            buf = cls._per_device.get(key)
+            if buf is None or buf.numel() < nbytes:
+                buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+                cls._per_device[key] = buf
+            return buf
+
+
+_F32, _BF16, _F8 = torch.float32, torch.bfloat16, torch.float8_e4m3fn
+
+
+def _check_tensor(t, name, shape, dtype):
+    if not isinstance(t, torch.Tensor):
+        raise ValueError(f"{name} must be a torch.Tensor")
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+    if t.dim() != len(shape):
+        raise ValueError(f"{name} must be {len(shape)}D, got {t.dim()}")
+    for i, (got, exp) in enumerate(zip(t.shape, shape)):
+        if got != exp:
+            raise ValueError(f"{name} shape mismatch at dim {i}: expected {exp}, got {got}")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} dtype mismatch: expected {dtype}, got {t.dtype}")
+
+
+def _validate(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+              gemm1_weights_scale, gemm2_weights, gemm2_weights_scale):
+    """Tensor contract of kernel.cu:1746-1769 with geometry derived from the shapes."""
+    if not isinstance(routing_logits, torch.Tensor) or routing_logits.dim() != 2:
+        raise ValueError("routing_logits must be 2D")
+    if not isinstance(gemm1_weights, torch.Tensor) or gemm1_weights.dim() != 3:
+        raise ValueError("gemm1_weights must be 3D")
+    T, E = routing_logits.shape
+    EL, two_i, H = gemm1_weights.shape
+    I = two_i // 2
+    if H % 128 or I % 128 or H == 0 or I == 0:
+        raise ValueError("gemm1_weights: hidden and intermediate sizes must be multiples of 128")
+    _check_tensor(routing_logits, "routing_logits", (T, E), _F32)
+    _check_tensor(routing_bias, "routing_bias", (E,), _BF16)
+    _check_tensor(hidden_states, "hidden_states", (T, H), _F8)
+    _check_tensor(hidden_states_scale, "hidden_states_scale", (H // 128, T), _F32)
+    _check_tensor(gemm1_weights, "gemm1_weights", (EL, 2 * I, H), _F8)
+    _check_tensor(gemm1_weights_scale, "gemm1_weights_scale", (EL, 2 * I // 128, H // 128), _F32)
+    _check_tensor(gemm2_weights, "gemm2_weights", (EL, H, I), _F8)
+    _check_tensor(gemm2_weights_scale, "gemm2_weights_scale", (EL, H // 128, I // 128), _F32)
+    dev = routing_logits.device
+    for name, t in (("routing_bias", routing_bias), ("hidden_states", hidden_states),
+                    ("hidden_states_scale", hidden_states_scale), ("gemm1_weights", gemm1_weights),
+                    ("gemm1_weights_scale", gemm1_weights_scale), ("gemm2_weights", gemm2_weights),
+                    ("gemm2_weights_scale", gemm2_weights_scale)):
+        if t.device != dev:
+            raise ValueError(f"routing_logits and {name} must be on the same device")
+    return T, E, EL, H, I
+
+
+def kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+           gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset: int,
+           routed_scaling_factor: float, *, out: torch.Tensor | None = None, tile_n: int = 0,
+           workspace: torch.Tensor | None = None, routing: tuple | None = None) -> torch.Tensor:
+    """Fused FP8 block-scaled DeepSeek-V3 MoE layer; returns bf16 [T, H].
+
+    Same positional signature as the reference ``kernel`` (kernel.cu:1727-1734). Extra
+    keyword-only arguments: ``out`` (destination), ``tile_n`` (override the autotune
+    table), ``workspace`` (caller scratch), ``routing`` ((n_group, topk_group, top_k)
+    override). Work is enqueued on the current torch stream; no host synchronisation.
+    """
+    T, E, EL, H, I = _validate(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                               gemm1_weights, gemm1_weights_scale, gemm2_weights,
+                               gemm2_weights_scale)
+    lib = load_library()
+    ng, kg, k = routing if routing is not None else (None, None, None)
+    prob = make_problem(T, E, EL, H, I, local_expert_offset, routed_scaling_factor, ng, kg, k,
+                        tile_n)
+    rc = lib.fmoe_validate(ctypes.byref(prob))
+    if rc != FMOE_OK:
+        _raise(lib, rc, "kernel")
+    dev = routing_logits.device
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    else:
+        _check_tensor(out, "out", (T, H), _BF16)
+    if T == 0:
+        return out
+    nbytes = workspace_bytes(prob)
+    if workspace is None:
+        with torch.cuda.device(dev):
+            workspace = Workspace.get(dev, nbytes)
+    tens = FmoeTensors(routing_logits.data_ptr(), routing_bias.data_ptr(),
+                       hidden_states.data_ptr(), hidden_states_scale.data_ptr(),
+                       gemm1_weights.data_ptr(), gemm1_weights_scale.data_ptr(),
+                       gemm2_weights.data_ptr(), gemm2_weights_scale.data_ptr(), out.data_ptr())
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = lib.fmoe_forward(ctypes.byref(prob), ctypes.byref(tens), workspace.data_ptr(),
+                              workspace.numel(), stream)
+    if rc != FMOE_OK:
+        _raise(lib, rc, "kernel")
+    return out
+
+
+def route(routing_logits: torch.Tensor, routing_bias: torch.Tensor, n_group: int,
+          topk_group: int, top_k: int, routed_scaling_factor: float, num_local_experts: int = 1,
+          local_expert_offset: int = 0):
+    """Routing kernel only: returns (topk_idx int32 [T, K], topk_w fp32 [T, K]) on device."""
+    T, E = routing_logits.shape
+    _check_tensor(routing_logits, "routing_logits", (T, E), _F32)
+    _check_tensor(routing_bias, "routing_bias", (E,), _BF16)
+    lib = load_library()
+    prob = make_problem(T, E, num_local_experts, 128, 128, local_expert_offset,
+                        routed_scaling_factor, n_group, topk_group, top_k)
+    dev = routing_logits.device
+    idx = torch.empty(T, top_k, dtype=torch.int32, device=dev)
+    w = torch.empty(T, top_k, dtype=torch.float32, device=dev)
+    if T == 0:
+        return idx, w
+    nbytes = workspace_bytes(prob)
+    ws = Workspace.get(dev, nbytes)
+    ro = FmoeRouteOut(idx.data_ptr(), w.data_ptr())
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = lib.fmoe_route(ctypes.byref(prob), routing_logits.data_ptr(), routing_bias.data_ptr(),
+                            ctypes.byref(ro), ws.data_ptr(), ws.numel(), stream)
+    if rc != FMOE_OK:
+        _raise(lib, rc, "route")
+    return idx, w
+
+
+def read_device_error(prob: FmoeProblem, workspace: torch.Tensor) -> int:
+    """Synchronise and return (and clear) the device error word of the last call."""
+    lib = load_library()
+    val = ctypes.c_int32(0)
+    stream = torch.cuda.current_stream(workspace.device).cuda_stream
+    rc = lib.fmoe_read_device_error(ctypes.byref(prob), workspace.data_ptr(), stream,
+                                    ctypes.byref(val))
+    if rc != FMOE_OK:
+        _raise(lib, rc, "read_device_error")
+    return int(val.value)
+
+
+def plan_view(prob: FmoeProblem, workspace: torch.Tensor) -> dict:
+    """Copies of the permutation the last call built (expert counts/offsets, row maps)."""
+    lib = load_library()
+    v = FmoePlanView()
+    rc = lib.fmoe_plan_view_get(ctypes.byref(prob), workspace.data_ptr(), ctypes.byref(v))
+    if rc != FMOE_OK:
+        _raise(lib, rc, "plan_view")
+    base = workspace.data_ptr()
+    w32 = workspace.view(torch.int32) if workspace.numel() % 4 == 0 else None
+
+    def grab(ptr, n):
+        off = (ptr - base) // 4
+        return w32[off:off + n].clone()
+
+    T, K, EL = prob.num_tokens, prob.top_k, prob.num_local_experts
+    return dict(expert_cnt=grab(v.expert_cnt, EL), expert_off=grab(v.expert_off, EL + 1),
+                row_token=grab(v.row_token, v.row_cap), token_row=grab(v.token_row, T * K),
+                meta=grab(v.meta, 16), row_cap=int(v.row_cap))
+
+
+class StageTimer:
+    """Records CUDA events at the six stage boundaries of every fmoe_forward() on this
+    thread (see fmoe_set_stage_events in include/fmoe.h); ``times_ms()`` returns the five
+    stage durations of the most recent call: route, permute, gemm1, gemm2, combine."""
+
+    STAGES = ("route", "permute", "gemm1", "gemm2", "combine")
+
+    def __init__(self):
+        self.events = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+        self._arr = (ctypes.c_void_p * 6)(*[e.cuda_event for e in self.events])
+
+    def __enter__(self):
+        lib = load_library()
+        rc = lib.fmoe_set_stage_events(ctypes.cast(self._arr, ctypes.c_void_p))
+        if rc != FMOE_OK:
+            _raise(lib, rc, "set_stage_events")
+        return self
+
+    def __exit__(self, *exc):
+        load_library().fmoe_set_stage_events(None)
+        return False
+
+    def times_ms(self):
+        return [self.events[i].elapsed_time(self.events[i + 1]) for i in range(5)]
+
+
+def load_tvm_ffi_kernel():
+    """The TVM-FFI `kernel` export (reference binding "tvm-ffi", kernel.cu:1839)."""
+    import tvm_ffi
+
+    load_library()
+    if not TVM_FFI_LIB_PATH.exists():
+        raise RuntimeError(f"TVM-FFI binding not built: {TVM_FFI_LIB_PATH}")
+    mod = tvm_ffi.load_module(str(TVM_FFI_LIB_PATH))
+    return mod["kernel"]

@@ -1,0 +1,140 @@
+/*
+ * fmoe.h -- C ABI of the B200-native fused FP8 block-scaled MoE operator.
+ *
+ * This is the drop-in boundary for the reference operator
+ *   ffi::Tensor kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+ *                      gemm1_weights, gemm1_weights_scale, gemm2_weights,
+ *                      gemm2_weights_scale, int32_t local_expert_offset,
+ *                      float routed_scaling_factor)
+ * of YuWei-CH/Fused-MoE-YWS solution/cuda/kernel.cu:1727-1734 (exported through TVM-FFI
+ * at kernel.cu:1839). The TVM-FFI binding in fused-moe-yws_b200/csrc/tvm_ffi_kernel.cc and
+ * the Python mirror in fused-moe-yws_b200/fmoe_b200 both call these functions.
+ *
+ * Conventions: plain device pointers and sizes, no framework types. Every function
+ * returns FMOE_OK or an error code; fmoe_last_error() gives the message of the most
+ * recent failure on the calling thread. The value/type/runtime split mirrors the
+ * reference's ValueError / TypeError / RuntimeError (kernel.cu:121-168, :53-62).
+ * Launches are asynchronous on the given stream; nothing synchronises the host.
+ */
+#ifndef FMOE_H_
+#define FMOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FMOE_ABI_VERSION 1
+
+enum fmoe_status {
+  FMOE_OK = 0,
+  FMOE_ERR_VALUE = 1,     /* bad shape, geometry, size or alignment (reference: ValueError) */
+  FMOE_ERR_TYPE = 2,      /* bad dtype code (reference: TypeError) */
+  FMOE_ERR_RUNTIME = 3,   /* CUDA launch / driver failure (reference: RuntimeError) */
+  FMOE_ERR_WORKSPACE = 4, /* workspace missing or too small */
+  FMOE_ERR_DEVICE = 5     /* a kernel reported an error word (timeout, overflow) */
+};
+
+/* Problem geometry. The reference hard-codes the DeepSeek-V3 values
+ * (kernel.cu:32-40); here they are runtime fields so the tiny contest geometry
+ * (H=256, I=128, 16 experts, 4 groups) runs through the same kernels. */
+typedef struct fmoe_problem {
+  int64_t num_tokens;          /* T: routing_logits.shape[0] */
+  int32_t num_experts;         /* E_global: routing_logits.shape[1] (<= 256, multiple of n_group) */
+  int32_t num_local_experts;   /* E_local: gemm1_weights.shape[0] (<= 64) */
+  int32_t hidden_size;         /* H: multiple of 128 */
+  int32_t intermediate_size;   /* I: multiple of 128 */
+  int32_t top_k;               /* experts per token (<= 32) */
+  int32_t n_group;             /* routing groups (<= 32) */
+  int32_t topk_group;          /* groups kept per token */
+  int32_t local_expert_offset; /* first global expert of this slice (kernel.cu:541) */
+  float routed_scaling_factor; /* multiplies the renormalised weights (kernel.cu:512) */
+  int32_t tile_n;              /* token tile of the grouped GEMMs; 0 = autotune table */
+} fmoe_problem;
+
+/* Device pointers, all contiguous, all on the current device; shapes as in
+ * kernel.cu:1746-1769. 8-bit float buffers hold E4M3 bytes; bf16 buffers hold raw bits.
+ * Base addresses must be 16-byte aligned (TMA). */
+typedef struct fmoe_tensors {
+  const float* routing_logits;      /* [T, E_global] fp32 */
+  const void* routing_bias;         /* [E_global] bf16 */
+  const void* hidden_states;        /* [T, H] e4m3 */
+  const float* hidden_states_scale; /* [H/128, T] fp32 (block-major, transposed) */
+  const void* gemm1_weights;        /* [E_local, 2I, H] e4m3 (rows [0,I) gate, [I,2I) up) */
+  const float* gemm1_weights_scale; /* [E_local, 2I/128, H/128] fp32 */
+  const void* gemm2_weights;        /* [E_local, H, I] e4m3 */
+  const float* gemm2_weights_scale; /* [E_local, H/128, I/128] fp32 */
+  void* output;                     /* [T, H] bf16, written completely */
+} fmoe_tensors;
+
+/* Routing outputs (device pointers) for fmoe_route(). */
+typedef struct fmoe_route_out {
+  int32_t* topk_idx; /* [T, top_k] global expert ids in selection order, -1 if unfilled */
+  float* topk_w;     /* [T, top_k] routed weights */
+} fmoe_route_out;
+
+/* Returns FMOE_ABI_VERSION. */
+int fmoe_abi_version(void);
+
+/* Message of the last failure on this thread ("" if none). */
+const char* fmoe_last_error(void);
+
+/* Geometry and argument checks without touching the device
+ * (replaces CheckTensor / CheckScalarVector, kernel.cu:121-168, for the size fields). */
+int fmoe_validate(const fmoe_problem* p);
+
+/* Scratch bytes fmoe_forward() needs for this problem. The reference keeps
+ * process-lifetime thread_local scratch caches instead (kernel.cu:234-270, :1784-1797);
+ * here the caller owns the workspace, so the library itself never allocates. */
+int fmoe_workspace_size(const fmoe_problem* p, size_t* bytes);
+
+/* Token tile (MMA N) the committed autotune table picks for num_tokens. */
+int fmoe_autotune_tile_n(int64_t num_tokens);
+
+/* The whole operator: routing -> permute/gather -> GEMM1+SwiGLU -> GEMM2 -> combine,
+ * writing bf16 [T, H] into t->output. Replaces kernel() at kernel.cu:1727-1837, minus its
+ * final cudaStreamSynchronize (kernel.cu:1834): everything is enqueued on `stream`
+ * (a cudaStream_t; NULL = legacy default stream). One call at a time per workspace. */
+int fmoe_forward(const fmoe_problem* p, const fmoe_tensors* t, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+/* Routing only (replaces sigmoid_bias_kernel + routing_select_kernel,
+ * kernel.cu:388-516), for parity tests and the expert-parallel dispatch.
+ * Needs the same workspace as fmoe_forward. */
+int fmoe_route(const fmoe_problem* p, const float* routing_logits, const void* routing_bias,
+               const fmoe_route_out* out, void* workspace, size_t workspace_bytes,
+               void* stream);
+
+/* Synchronises `stream`, then reads and clears the device error word the kernels of the
+ * last call on this workspace wrote (bitmask of timeouts / overflow; 0 = clean). */
+int fmoe_read_device_error(const fmoe_problem* p, void* workspace, void* stream,
+                           int32_t* device_error);
+
+/* Stage timing: when `events` is non-NULL, every later fmoe_forward() on this thread
+ * records events[0..5] (cudaEvent_t handles owned by the caller) on its stream at the
+ * stage boundaries: start, after routing, after permute/gather, after GEMM1+SwiGLU,
+ * after GEMM2, after combine. NULL turns recording off. The reference's profiling hook
+ * (FUSED_MOE_PROFILE, set by scripts/run_modal.py:106-116) is never read by kernel.cu;
+ * this one is live. */
+int fmoe_set_stage_events(void* const* events);
+
+/* Debug view of the permutation of the last call (device pointers into the workspace):
+ * expert counts [E_local], expert offsets [E_local+1], row->token [row_cap],
+ * (token,k)->row [T*top_k], and row_cap. For parity tests of the permute kernel. */
+typedef struct fmoe_plan_view {
+  const int32_t* expert_cnt;
+  const int32_t* expert_off;
+  const int32_t* row_token;
+  const int32_t* token_row;
+  const int32_t* meta;
+  int64_t row_cap;
+} fmoe_plan_view;
+int fmoe_plan_view_get(const fmoe_problem* p, void* workspace, fmoe_plan_view* view);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FMOE_H_ */
