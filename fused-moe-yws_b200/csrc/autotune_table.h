@@ -20,15 +20,13 @@ struct TileChoice {
 constexpr TileChoice kAutotuneTable[] = {
     {256, 16},
     {512, 32},
-    {1024, 64},
-    {2048, 128},
-    {INT64_MAX, 256},
+    {INT64_MAX, 64},
 };
 
 inline int autotune_tile_n(int64_t num_tokens) {
   for (const TileChoice& c : kAutotuneTable)
     if (num_tokens <= c.max_tokens) return c.tile_n;
-  return 256;
+  return 64;
 }
 
 }  // namespace fmoe

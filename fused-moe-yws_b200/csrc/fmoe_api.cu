@@ -75,14 +75,14 @@ int validate(const fmoe_problem* p) {
     return fail(FMOE_ERR_VALUE, "top_k must be in [1, 32] and fit in the kept groups");
   if (p->num_local_experts < 1 || p->num_local_experts > 64)
     return fail(FMOE_ERR_VALUE, "num_local_experts must be in [1, 64]");
-  if (p->hidden_size < 128 || p->hidden_size % 128 != 0 || p->hidden_size > 65536)
-    return fail(FMOE_ERR_VALUE, "hidden_size must be a positive multiple of 128 (<= 65536)");
+  if (p->hidden_size < 128 || p->hidden_size % 128 != 0 || p->hidden_size > 16384)
+    return fail(FMOE_ERR_VALUE, "hidden_size must be a positive multiple of 128 (<= 16384)");
   if (p->intermediate_size < 128 || p->intermediate_size % 128 != 0 ||
-      p->intermediate_size > 65536)
+      p->intermediate_size > 16384)
     return fail(FMOE_ERR_VALUE,
-                "intermediate_size must be a positive multiple of 128 (<= 65536)");
+                "intermediate_size must be a positive multiple of 128 (<= 16384)");
   if (p->tile_n != 0 && !gemm_bn_supported(p->tile_n))
-    return fail(FMOE_ERR_VALUE, "tile_n must be 0 or one of 16, 32, 64, 128, 256");
+    return fail(FMOE_ERR_VALUE, "tile_n must be 0 or one of 16, 32, 64");
   const WorkspaceLayout L = make_layout(to_geometry(*p));
   if (L.row_cap * (int64_t)p->hidden_size >= ((int64_t)1 << 40))
     return fail(FMOE_ERR_VALUE, "problem too large for the row-permuted workspace");
@@ -180,6 +180,8 @@ RouteArgs route_args(const fmoe_problem* p, const Carved& c, const float* logits
   a.local_offset = p->local_expert_offset;
   a.rsf = p->routed_scaling_factor;
   a.bn = bn;
+  a.bn_log2 = 0;
+  while ((1 << a.bn_log2) < bn) ++a.bn_log2;
   a.row_cap = c.L.row_cap;
   a.max_chunks = c.L.max_chunks;
   a.topk_idx = c.at<int>(c.L.topk_idx);
@@ -195,7 +197,9 @@ RouteArgs route_args(const fmoe_problem* p, const Carved& c, const float* logits
 
 int launch_route(const fmoe_problem* p, const Carved& c, const float* logits, const void* bias,
                  int bn, cudaStream_t stream) {
-  FMOE_CUDA_TRY(cudaMemsetAsync(c.at<int>(c.L.meta), 0, kMetaWords * sizeof(int), stream));
+  // meta words and the split-K counters are contiguous: one small memset per call
+  FMOE_CUDA_TRY(cudaMemsetAsync(c.at<int>(c.L.meta), 0, c.L.counters - c.L.meta +
+                                kTileCounters * sizeof(int), stream));
   const RouteArgs ra = route_args(p, c, logits, bias, bn);
   route_plan_kernel<<<(unsigned)c.L.n_route_ctas, kRouteTokensPerCta * 32, 0, stream>>>(ra);
   FMOE_CUDA_TRY(cudaGetLastError());
@@ -273,19 +277,25 @@ extern "C" int fmoe_forward(const fmoe_problem* p, const fmoe_tensors* t, void* 
   sa.a_perm = c.at<uint8_t>(c.L.a_perm);
   sa.a_scale = c.at<float>(c.L.a_scale);
   sa.meta = c.at<int>(c.L.meta);
-  scatter_gather_kernel<<<(unsigned)c.L.n_route_ctas, 256, 0, stream>>>(sa);
+  {
+    // split each row's columns over enough CTAs to cover the SMs at small T
+    const int sms = num_sms_current();
+    int parts = (int)((2 * sms + c.L.n_route_ctas - 1) / c.L.n_route_ctas);
+    parts = parts < 1 ? 1 : (parts > 28 ? 28 : parts);
+    scatter_gather_kernel<<<dim3((unsigned)c.L.n_route_ctas, (unsigned)parts), 256, 0, stream>>>(sa);
+  }
   FMOE_CUDA_TRY(cudaGetLastError());
   if ((v = mark_stage(2, stream)) != FMOE_OK) return v;
 
   CUtensorMap m_w13, m_a, m_w2, m_cq;
-  if ((v = make_map(&m_w13, t->gemm1_weights, H, (uint64_t)EL * 2 * I, H, 128, 64,
+  if ((v = make_map(&m_w13, t->gemm1_weights, H, (uint64_t)EL * 2 * I, H, 128, 128,
                     CU_TENSOR_MAP_SWIZZLE_128B, "gemm1_weights")) != FMOE_OK)
     return v;
   if ((v = make_map(&m_a, sa.a_perm, H, c.L.row_cap, H, 128, bn, CU_TENSOR_MAP_SWIZZLE_128B,
                     "permuted activations")) != FMOE_OK)
     return v;
-  if ((v = make_map(&m_w2, t->gemm2_weights, I, (uint64_t)EL * H, I, 64, 128,
-                    CU_TENSOR_MAP_SWIZZLE_64B, "gemm2_weights")) != FMOE_OK)
+  if ((v = make_map(&m_w2, t->gemm2_weights, I, (uint64_t)EL * H, I, 128, 128,
+                    CU_TENSOR_MAP_SWIZZLE_128B, "gemm2_weights")) != FMOE_OK)
     return v;
   uint8_t* cq = c.at<uint8_t>(c.L.cq);
   if ((v = make_map(&m_cq, cq, 2 * (uint64_t)I, c.L.row_cap, 2 * (uint64_t)I, 128, bn,
@@ -303,9 +313,11 @@ extern "C" int fmoe_forward(const fmoe_problem* p, const fmoe_tensors* t, void* 
   g.row_w = c.at<float>(c.L.row_w);
   g.ow = c.at<__nv_bfloat16>(c.L.ow);
   g.err = c.at<int>(c.L.meta) + kMetaError;
-  const int sms = num_sms_current();
+  g.partials = c.at<float>(c.L.partials);
+  g.tile_counters = c.at<int>(c.L.counters);
+  const int sms = num_sms_current() < kMaxSms ? num_sms_current() : kMaxSms;
 
-  g.m_tiles = I / 64;
+  g.m_tiles = I / kBlock;
   g.k_steps = H / kBlock;
   g.w_scale = t->gemm1_weights_scale;
   g.act_scale = sa.a_scale;
@@ -314,7 +326,7 @@ extern "C" int fmoe_forward(const fmoe_problem* p, const fmoe_tensors* t, void* 
   if ((v = mark_stage(3, stream)) != FMOE_OK) return v;
 
   g.m_tiles = H / kBlock;
-  g.k_steps = I / 64;
+  g.k_steps = I / kBlock;
   g.w_scale = t->gemm2_weights_scale;
   g.act_scale = g.c_scale;
   bound = c.L.max_chunks * (int64_t)g.m_tiles;
@@ -328,7 +340,7 @@ extern "C" int fmoe_forward(const fmoe_problem* p, const fmoe_tensors* t, void* 
   ca.T = T;
   ca.H = H;
   ca.top_k = p->top_k;
-  combine_kernel<<<(unsigned)T, 128, 0, stream>>>(ca);
+  combine_kernel<<<dim3((unsigned)T, (unsigned)((H / 8 + 127) / 128)), 128, 0, stream>>>(ca);
   FMOE_CUDA_TRY(cudaGetLastError());
   return mark_stage(5, stream);
 }

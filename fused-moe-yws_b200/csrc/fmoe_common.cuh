@@ -31,7 +31,10 @@ enum MetaSlot : int {
 constexpr int kBlock = 128;        // FP8 block-scale granularity
 constexpr int kRowAlign = 16;      // expert row segments padded to the MMA N granularity
 constexpr int kRouteTokensPerCta = 16;  // one warp per token in the routing kernel
-constexpr int kMaxBN = 256;        // largest token tile (MMA N) the GEMMs use
+constexpr int kMaxBN = 64;         // largest token tile (MMA N) the GEMMs use
+constexpr int kMaxSms = 160;       // upper bound on SMs per GPU for split-K scratch sizing
+constexpr int kMaxSplit = 8;       // split-K factor cap
+constexpr int kTileCounters = 4 * kMaxSms;  // split-K arrival counters (tiles < 2 x SMs)
 
 struct Geometry {
   int64_t T;          // tokens
@@ -58,7 +61,7 @@ struct WorkspaceLayout {
   int64_t max_chunks;
   int64_t n_route_ctas;
   size_t topk_idx, topk_w, token_row, cta_counts, cta_base, expert_cnt, expert_off, meta, chunks,
-      row_token, row_w, a_perm, a_scale, cq, c_scale, ow;
+      row_token, row_w, a_perm, a_scale, cq, c_scale, ow, counters, partials;
   size_t total;
 };
 
@@ -85,14 +88,16 @@ inline WorkspaceLayout make_layout(const Geometry& g) {
   L.expert_cnt = take((size_t)g.E_local * 4);
   L.expert_off = take((size_t)(g.E_local + 1) * 4);
   L.meta = take(kMetaWords * 4);
+  L.counters = take((size_t)kTileCounters * 4);  // right after meta: zeroed together
   L.chunks = take((size_t)L.max_chunks * sizeof(Chunk));
   L.row_token = take((size_t)L.row_cap * 4);
   L.row_w = take((size_t)L.row_cap * 4);
   L.a_perm = take((size_t)L.row_cap * g.H);
   L.a_scale = take((size_t)(g.H / kBlock) * L.row_cap * 4);
   L.cq = take((size_t)L.row_cap * 2 * g.I);
-  L.c_scale = take((size_t)(g.I / 64) * L.row_cap * 4);
+  L.c_scale = take((size_t)(g.I / kBlock) * L.row_cap * 4);
   L.ow = take((size_t)L.row_cap * g.H * 2);
+  L.partials = take((size_t)4 * kMaxSms * 2 * 128 * kMaxBN * 4);
   L.total = off;
   return L;
 }

@@ -15,7 +15,8 @@ struct RouteArgs {
   int64_t T;
   int E, n_group, topk_group, top_k, E_local, local_offset;
   float rsf;
-  int bn;                  // token tile of the grouped GEMMs (chunk size)
+  int bn;                  // token tile of the grouped GEMMs (chunk size, a power of two)
+  int bn_log2;
   int64_t row_cap, max_chunks;
   int* topk_idx;           // [T, K]
   float* topk_w;           // [T, K]
@@ -49,19 +50,21 @@ struct ScatterArgs {
 struct GemmArgs {
   const Chunk* chunks;
   const int* meta;
-  int m_tiles;             // weight-row tiles per expert (I/64 for GEMM1, H/128 for GEMM2)
-  int k_steps;             // H/128 (GEMM1) or I/64 (GEMM2)
+  int m_tiles;             // weight-row tiles per expert (I/128 for GEMM1, H/128 for GEMM2)
+  int k_steps;             // 128-wide K steps: H/128 (GEMM1) or I/128 (GEMM2)
   int H, I;
   int64_t row_cap;         // leading dimension of the activation scale arrays
   const float* w_scale;    // [E_local, rows/128, cols/128]
-  const float* act_scale;  // GEMM1: a_scale [H/128, row_cap]; GEMM2: c_scale [I/64, row_cap]
+  const float* act_scale;  // GEMM1: a_scale [H/128, row_cap]; GEMM2: c_scale [I/128, row_cap]
   // GEMM1 outputs
-  uint8_t* cq;             // [row_cap, 2I]: per 64-column block j, 64 hi bytes then 64 lo bytes
-  float* c_scale;          // [I/64, row_cap]
+  uint8_t* cq;             // [row_cap, 2I]: per 128-column block j, 128 hi bytes then 128 lo
+  float* c_scale;          // [I/128, row_cap]
   // GEMM2 inputs / outputs
   const float* row_w;      // [row_cap]
   __nv_bfloat16* ow;       // [row_cap, H] weighted expert outputs
   int* err;                // device error word
+  float* partials;         // split-K partial tiles
+  int* tile_counters;      // split-K arrival counters (self-resetting, zeroed per call)
 };
 
 struct CombineArgs {
@@ -82,5 +85,6 @@ cudaError_t launch_gemm1(int bn, const CUtensorMap& w13_map, const CUtensorMap& 
 cudaError_t launch_gemm2(int bn, const CUtensorMap& w2_map, const CUtensorMap& cq_map,
                          const GemmArgs& args, int grid, cudaStream_t stream);
 bool gemm_bn_supported(int bn);
+size_t gemm_partial_bytes();
 
 }  // namespace fmoe

@@ -43,26 +43,41 @@ namespace {
 
 constexpr int kThreads = 320;
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in dynamic shared memory per CTA
+constexpr int kMaxKSteps = 128;     // H/128 and I/128 are validated <= 128
+constexpr int kEpiThreads = 256;    // warps 2..9
+constexpr int kBarAll = 3;          // named barrier id over all epilogue warps
 
 template <int BN, bool kG1>
 struct Cfg {
-  static constexpr int kAK = kG1 ? 128 : 64;                 // weight K bytes per step
-  static constexpr int kASwz = kG1 ? 128 : 64;
-  static constexpr int kABytes = 128 * kAK;
-  static constexpr int kBBytes = BN * 128;                   // token K bytes per step = 128
+  static constexpr int kAcc = kG1 ? 2 : 1;                    // accumulators per K step
+  static constexpr int kABytes = kG1 ? 2 * 128 * 128 : 128 * 128;  // gate+up or W2 rows
+  static constexpr int kBBytes = (kG1 ? 1 : 2) * BN * 128;   // tokens (G2: hi and lo)
   static constexpr int kStageBytes = kABytes + kBBytes;
-  static constexpr int HB = BN / 2;                          // columns per epilogue half
-  static constexpr int CW = HB < 32 ? HB : 32;               // TMEM load width
-  static constexpr int kExBytes = kG1 ? 2 * 64 * 33 * 4 : 0; // SwiGLU exchange (padded)
-  static constexpr int kCbufBytes = 2 * 2 * 2 * HB * 4;      // [parity][half][gate/up][col]
-  static constexpr int kBarBytes = 512;
-  static constexpr int kFixed = 1024 + kExBytes + kCbufBytes + kBarBytes;
-  static constexpr int kStagesRaw = (kSmemLimit - kFixed) / kStageBytes;
+  static constexpr int HB = BN / 2;                           // token columns per half
+  static constexpr int CW = HB < 32 ? HB : 32;                // TMEM load width
+  static constexpr int kBNs = BN < 32 ? 32 : BN;              // TMEM column stride
+  static constexpr int kBufCols = kAcc * kBNs;
+  static constexpr int kNBufRaw = 512 / kBufCols;
+  static constexpr int kNBuf = kNBufRaw > 8 ? 8 : kNBufRaw;   // accumulator ring depth
+  static constexpr int kExBytes = kG1 ? 2 * 128 * (CW + 1) * 4 : 0;  // SwiGLU staging
+  static constexpr int kWscBytes = 2 * kMaxKSteps * 4;        // [gate/up][k step]
+  static constexpr int kSlotBytes = BN * 4;                   // act scales of one K step
+  static constexpr int kMaxSlots = 16 + 8 + 2;
+  static constexpr int kBarBytes = 1024;
+  static constexpr int kFixedMax =
+      1024 + kExBytes + kWscBytes + kMaxSlots * kSlotBytes + kBarBytes + 64;
+  static constexpr int kStagesRaw = (kSmemLimit - kFixedMax) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 16 ? 16 : kStagesRaw;
+  static constexpr int kSlots = kStages + kNBuf + 2;          // scale ring depth
+  static constexpr int kFixed =
+      1024 + kExBytes + kWscBytes + kSlots * kSlotBytes + kBarBytes + 64;
   static constexpr int kSmemBytes = kFixed + kStages * kStageBytes;
   static constexpr uint32_t kTx = kStageBytes;
+  static constexpr int kPartialFloats = kAcc * 128 * BN;      // one split-K partial tile
   static_assert(kStages >= 2, "not enough shared memory for a 2-stage pipeline");
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
+  static_assert((16 + 16 + 8 + 8 + 2 * kMaxSlots + 3) * 8 <= kBarBytes, "barrier area");
+  static_assert(kNBuf >= 2, "need at least two accumulator buffers");
 };
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
@@ -72,28 +87,60 @@ __device__ __forceinline__ void set_error(int* err, volatile int* abort_flag, in
   *abort_flag = 1;
 }
 
+// Split-K factor for this launch: enough work units to cover every SM about twice
+// when the tile count alone cannot; identical in every CTA and role.
+__device__ __forceinline__ int split_factor(int num_tiles, int ks_total) {
+  if (num_tiles <= 0) return 1;
+  int s = (2 * (int)gridDim.x + num_tiles - 1) / num_tiles;
+  s = s < 1 ? 1 : s;
+  s = s > kMaxSplit ? kMaxSplit : s;
+  return s > ks_total ? ks_total : s;
+}
+
+// Promote one accumulator: acc[j] += D[row, col_j] * scale_j * sw for this thread's
+// half of the token columns (only column chunks below ncols are read).
+template <int HB, int CW>
+__device__ __forceinline__ void promote(float (&acc)[HB], uint32_t taddr, const float* sa,
+                                        float sw, int col0, int ncols) {
+#pragma unroll
+  for (int c = 0; c < HB / CW; ++c) {
+    if (col0 + c * CW < ncols) {
+      uint32_t v[CW];
+      tmem_ld_32x32b<CW>(taddr + c * CW, v);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < CW; ++i)
+        acc[c * CW + i] = fmaf(__uint_as_float(v[i]), sa[c * CW + i] * sw, acc[c * CW + i]);
+    }
+  }
+}
+
 template <int BN, bool kG1>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
   using C = Cfg<BN, kG1>;
-  constexpr int S = C::kStages, HB = C::HB, CW = C::CW;
+  constexpr int S = C::kStages, HB = C::HB, CW = C::CW, NB = C::kNBuf, SR = C::kSlots;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   uint8_t* stages = smem;
-  float* ex = reinterpret_cast<float*>(smem + S * C::kStageBytes);
-  float* cbuf = reinterpret_cast<float*>(smem + S * C::kStageBytes + C::kExBytes);
-  uint64_t* bars =
-      reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes + C::kExBytes + C::kCbufBytes);
-  uint64_t* full = bars;            // [S]
-  uint64_t* empty = bars + 16;      // [S]
-  uint64_t* tfull = bars + 32;      // [2]
-  uint64_t* tempty = bars + 34;     // [2]
-  uint64_t* mma_done = bars + 36;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 38);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 39);
-  static_assert(40 * 8 <= C::kBarBytes, "barrier area");
+  uint8_t* fixed = smem + S * C::kStageBytes;
+  float* ex = reinterpret_cast<float*>(fixed);
+  float* wsc = reinterpret_cast<float*>(fixed + C::kExBytes);
+  float* sring = reinterpret_cast<float*>(fixed + C::kExBytes + C::kWscBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(fixed + C::kExBytes + C::kWscBytes +
+                                               SR * C::kSlotBytes);
+  uint64_t* full = bars;                 // [S]   TMA -> MMA
+  uint64_t* empty = bars + 16;           // [S]   MMA -> TMA
+  uint64_t* tfull = bars + 32;           // [NB]  MMA -> epilogue
+  uint64_t* tempty = bars + 40;          // [NB]  epilogue -> MMA
+  uint64_t* sfull = bars + 48;           // [SR]  scale ring, TMA -> epilogue
+  uint64_t* sempty = sfull + C::kMaxSlots;  // [SR] epilogue -> TMA
+  uint64_t* mma_done = sempty + C::kMaxSlots;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(mma_done + 2);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(mma_done + 2) + 1;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -101,9 +148,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NB; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 8);
+    }
+    for (int r = 0; r < SR; ++r) {
+      mbar_init(&sfull[r], 1);
+      mbar_init(&sempty[r], 8);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -124,6 +175,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int num_tiles = args.meta[kMetaNumChunks] * args.m_tiles;
   const int KS = args.k_steps;
+  const int SPLIT = split_factor(num_tiles, KS);
+  const int num_units = num_tiles * SPLIT;
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -132,12 +185,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_a = policy_evict_last();   // token tiles: re-read by every m tile
       int it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
+        const int tile = unit / SPLIT, sp = unit % SPLIT;
         const Chunk ch = args.chunks[tile / args.m_tiles];
         const int m = tile % args.m_tiles;
-        for (int ks = 0; ks < KS; ++ks, ++it) {
-          const int s = it % S;
-          if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, abort_flag)) {
+        const int k0 = KS * sp / SPLIT, k1 = KS * (sp + 1) / SPLIT;
+        const float* asrc = args.act_scale + ch.row0;
+        for (int ks = k0; ks < k1; ++ks, ++it) {
+          const int s = it % S, slot = it % SR;
+          if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, abort_flag) ||
+              !mbar_wait(&sempty[slot], ((it / SR) & 1) ^ 1, abort_flag)) {
             ok = false;
             break;
           }
@@ -145,33 +202,43 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sb = sa + C::kABytes;
           mbar_arrive_expect_tx(&full[s], C::kTx);
           if constexpr (kG1) {
-            const int wrow = ch.expert * 2 * args.I + m * 64;
+            const int wrow = ch.expert * 2 * args.I + m * 128;
             tma_load_2d(sa, &tmA, &full[s], ks * 128, wrow, pol_w);
-            tma_load_2d(sa + 64 * 128, &tmA, &full[s], ks * 128, wrow + args.I, pol_w);
+            tma_load_2d(sa + 128 * 128, &tmA, &full[s], ks * 128, wrow + args.I, pol_w);
+            tma_load_2d(sb, &tmB, &full[s], ks * 128, ch.row0, pol_a);
           } else {
             const int wrow = ch.expert * args.H + m * 128;
-            tma_load_2d(sa, &tmA, &full[s], ks * 64, wrow, pol_w);
+            tma_load_2d(sa, &tmA, &full[s], ks * 128, wrow, pol_w);
+            tma_load_2d(sb, &tmB, &full[s], ks * 256, ch.row0, pol_a);             // hi
+            tma_load_2d(sb + BN * 128, &tmB, &full[s], ks * 256 + 128, ch.row0, pol_a);  // lo
           }
-          tma_load_2d(sb, &tmB, &full[s], ks * 128, ch.row0, pol_a);
+          // activation / intermediate scales of this K step for the chunk's columns
+          mbar_arrive_expect_tx(&sfull[slot], ch.ncols * 4);
+          bulk_load_1d(sring + slot * BN, asrc + (int64_t)ks * args.row_cap, ch.ncols * 4,
+                       &sfull[slot]);
         }
       }
       if (!ok) set_error(args.err, abort_flag, kErrTimeoutProducer);
-      // drain: every issued load must land before the CTA's shared memory is released
+      // drain: every issued copy must land before the CTA's shared memory is released
       static const int zero = 0;
       for (int j = it > S ? it - S : 0; j < it; ++j)
         mbar_wait(&full[j % S], (j / S) & 1, &zero);
+      for (int j = it > SR ? it - SR : 0; j < it; ++j)
+        mbar_wait(&sfull[j % SR], (j / SR) & 1, &zero);
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      int it = 0, acc_it = 0;
+      int it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
+        const int tile = unit / SPLIT, sp = unit % SPLIT;
         const Chunk ch = args.chunks[tile / args.m_tiles];
         const uint32_t idesc = idesc_e4m3_f32(128, ch.ncols);
-        for (int ks = 0; ks < KS; ++ks, ++it, ++acc_it) {
-          const int b = acc_it & 1, use = acc_it >> 1;
+        const int k0 = KS * sp / SPLIT, k1 = KS * (sp + 1) / SPLIT;
+        for (int ks = k0; ks < k1; ++ks, ++it) {
+          const int b = it % NB, use = it / NB;
           if (!mbar_wait(&tempty[b], (use & 1) ^ 1, abort_flag)) {
             ok = false;
             break;
@@ -183,19 +250,25 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           const uint32_t sa = smem_addr(stages + s * C::kStageBytes);
-          const uint64_t adesc = smem_desc_kmajor(sa, C::kASwz);
-          const uint64_t bdesc = smem_desc_kmajor(sa + C::kABytes, 128);
-          const uint32_t d = tmem + b * 256;
+          const uint32_t d = tmem + b * C::kBufCols;
           if constexpr (kG1) {
+            const uint64_t ag = smem_desc_kmajor(sa, 128);
+            const uint64_t au = smem_desc_kmajor(sa + 128 * 128, 128);
+            const uint64_t bd = smem_desc_kmajor(sa + C::kABytes, 128);
 #pragma unroll
-            for (int sub = 0; sub < 4; ++sub)
-              mma_f8f6f4(d, adesc + 2 * sub, bdesc + 2 * sub, idesc, sub > 0);
+            for (int sub = 0; sub < 4; ++sub) {
+              mma_f8f6f4(d, ag + 2 * sub, bd + 2 * sub, idesc, sub > 0);
+              mma_f8f6f4(d + C::kBNs, au + 2 * sub, bd + 2 * sub, idesc, sub > 0);
+            }
           } else {
-            // hi half of the C block, then the lo half, same W2 block, same accumulator
-            mma_f8f6f4(d, adesc + 0, bdesc + 0, idesc, 0);
-            mma_f8f6f4(d, adesc + 2, bdesc + 2, idesc, 1);
-            mma_f8f6f4(d, adesc + 0, bdesc + 4, idesc, 1);
-            mma_f8f6f4(d, adesc + 2, bdesc + 6, idesc, 1);
+            // hi and lo parts of the 128-column C block share one scale -> one accumulator
+            const uint64_t ad = smem_desc_kmajor(sa, 128);
+            const uint64_t bh = smem_desc_kmajor(sa + C::kABytes, 128);
+            const uint64_t bl = smem_desc_kmajor(sa + C::kABytes + BN * 128, 128);
+#pragma unroll
+            for (int sub = 0; sub < 4; ++sub) mma_f8f6f4(d, ad + 2 * sub, bh + 2 * sub, idesc, sub > 0);
+#pragma unroll
+            for (int sub = 0; sub < 4; ++sub) mma_f8f6f4(d, ad + 2 * sub, bl + 2 * sub, idesc, 1);
           }
           tc_commit(&empty[s]);
           tc_commit(&tfull[b]);
@@ -214,135 +287,164 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;           // TMEM lane quadrant this warp may access
     const int half = ew >> 2;         // token column half
     const int tid_h = (ew & 3) * 32 + lane;
+    const int tid_e = ew * 32 + lane;  // 0..255
     const int r = q * 32 + lane;      // accumulator row = weight row inside the tile
-    const int bar_id = 1 + half;      // named barrier of the 4 warps of this half
-    float acc[HB];
-    int acc_it = 0;
+    const int bar_half = 1 + half;    // named barrier of the 4 warps of this half
+    float acc_g[HB];
+    float acc_u[kG1 ? HB : 1];
+    int it = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+    for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x) {
+      const int tile = unit / SPLIT, sp = unit % SPLIT;
       const Chunk ch = args.chunks[tile / args.m_tiles];
       const int m = tile % args.m_tiles;
       const int ncols = ch.ncols;
-#pragma unroll
-      for (int j = 0; j < HB; ++j) acc[j] = 0.0f;
-      // scale rows of the weight tile
-      const float* ws_gate;
-      const float* ws_up;
-      int ws_step;
-      if constexpr (kG1) {
-        const int nb2 = 2 * args.I / kBlock, kbh = args.H / kBlock;
-        ws_gate = args.w_scale + ((int64_t)ch.expert * nb2 + (m * 64) / kBlock) * kbh;
-        ws_up = args.w_scale + ((int64_t)ch.expert * nb2 + (args.I + m * 64) / kBlock) * kbh;
-        ws_step = 1;
-      } else {
-        const int nbh = args.H / kBlock, kbi = args.I / kBlock;
-        ws_gate = args.w_scale + ((int64_t)ch.expert * nbh + m) * kbi;
-        ws_up = ws_gate;
-        ws_step = 2;  // one W2 scale column per two 64-column C blocks
-      }
-      for (int ks = 0; ks < KS; ++ks, ++acc_it) {
-        const int par = acc_it & 1;
-        float* cb_half = cbuf + (par * 2 + half) * 2 * HB;
-        // combined per-column scale for this K block: w_scale(row block) * act_scale(token)
-        {
-          const float wg = __ldg(ws_gate + ks / ws_step);
-          const float wu = __ldg(ws_up + ks / ws_step);
-          const float* as = args.act_scale + (int64_t)ks * args.row_cap + ch.row0 + half * HB;
-          for (int idx = tid_h; idx < 2 * HB; idx += 128) {
-            const int g = idx / HB, col = idx - g * HB;
-            const float sa = (half * HB + col < ncols) ? __ldg(as + col) : 0.0f;
-            cb_half[idx] = (g == 0 ? wg : wu) * sa;
-          }
+      const int k0 = KS * sp / SPLIT, k1 = KS * (sp + 1) / SPLIT;
+      // weight block scales of this tile (one row for W2, gate and up rows for W13)
+      named_bar(kBarAll, kEpiThreads);
+      {
+        const int kbh = (kG1 ? args.H : args.I) / kBlock;
+        const float* g;
+        const float* u;
+        if constexpr (kG1) {
+          const int nb2 = 2 * args.I / kBlock;
+          g = args.w_scale + ((int64_t)ch.expert * nb2 + m) * kbh;
+          u = args.w_scale + ((int64_t)ch.expert * nb2 + args.I / kBlock + m) * kbh;
+        } else {
+          g = args.w_scale + ((int64_t)ch.expert * (args.H / kBlock) + m) * kbh;
+          u = g;
         }
-        const int b = acc_it & 1, use = acc_it >> 1;
-        const bool good = mbar_wait(&tfull[b], use & 1, abort_flag);
-        if (named_bar_or(bar_id, 128, !good)) {
+        for (int i = tid_e; i < 2 * kbh; i += kEpiThreads)
+          wsc[(i >= kbh) * kMaxKSteps + (i % kbh)] = __ldg((i >= kbh ? u : g) + (i % kbh));
+      }
+      named_bar(kBarAll, kEpiThreads);
+#pragma unroll
+      for (int j = 0; j < HB; ++j) acc_g[j] = 0.0f;
+      if constexpr (kG1) {
+#pragma unroll
+        for (int j = 0; j < HB; ++j) acc_u[j] = 0.0f;
+      }
+      for (int ks = k0; ks < k1; ++ks, ++it) {
+        const int b = it % NB, use = it / NB;
+        const int slot = it % SR, suse = it / SR;
+        if (!ok) continue;
+        if (!mbar_wait(&sfull[slot], suse & 1, abort_flag) ||
+            !mbar_wait(&tfull[b], use & 1, abort_flag)) {
           ok = false;
-          break;
+          continue;
         }
         tc_fence_after();
-        const float* cb = cb_half + ((kG1 && q >= 2) ? HB : 0);
-        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + b * 256 + half * HB;
-#pragma unroll
-        for (int c = 0; c < HB / CW; ++c) {
-          if (half * HB + c * CW < ncols) {
-            uint32_t v[CW];
-            tmem_ld_32x32b<CW>(tbase + c * CW, v);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < CW; ++i)
-              acc[c * CW + i] = fmaf(__uint_as_float(v[i]), cb[c * CW + i], acc[c * CW + i]);
-          }
-        }
+        const float* sa = sring + slot * BN + half * HB;
+        const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + b * C::kBufCols + half * HB;
+        promote<HB, CW>(acc_g, tb, sa, wsc[ks], half * HB, ncols);
+        if constexpr (kG1) promote<HB, CW>(acc_u, tb + C::kBNs, sa, wsc[kMaxKSteps + ks], half * HB, ncols);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[b]);
+        if (lane == 0) {
+          mbar_arrive(&tempty[b]);
+          mbar_arrive(&sempty[slot]);
+        }
       }
-      if (!ok) break;
+      // one abort decision for all epilogue warps (nobody waits at a barrier alone)
+      if (named_bar_or(kBarAll, kEpiThreads, !ok)) {
+        ok = false;
+        break;
+      }
+
+      // ---- split-K: publish this unit's partial; the last unit of the tile finishes ----
+      if (SPLIT > 1) {
+        float* part = args.partials + (int64_t)unit * C::kPartialFloats;
+#pragma unroll
+        for (int j = 0; j < HB; ++j) part[(0 * 128 + r) * BN + half * HB + j] = acc_g[j];
+        if constexpr (kG1) {
+#pragma unroll
+          for (int j = 0; j < HB; ++j) part[(1 * 128 + r) * BN + half * HB + j] = acc_u[j];
+        }
+        __threadfence();
+        named_bar(kBarAll, kEpiThreads);
+        if (tid_e == 0) {
+          const int done = atomicAdd(args.tile_counters + tile, 1);
+          const bool last = done == SPLIT - 1;
+          if (last) args.tile_counters[tile] = 0;  // ready for the next launch
+          *last_flag = last;
+        }
+        named_bar(kBarAll, kEpiThreads);
+        if (!*last_flag) continue;
+        __threadfence();
+        // deterministic: sum the partials in split order
+        const float* base = args.partials + (int64_t)(tile * SPLIT) * C::kPartialFloats;
+#pragma unroll
+        for (int j = 0; j < HB; ++j) {
+          float s0 = 0.0f, s1 = 0.0f;
+          for (int s2 = 0; s2 < SPLIT; ++s2) {
+            const float* pp = base + (int64_t)s2 * C::kPartialFloats;
+            s0 += (s2 == sp) ? acc_g[j] : __ldcg(pp + (0 * 128 + r) * BN + half * HB + j);
+            if constexpr (kG1)
+              s1 += (s2 == sp) ? acc_u[j] : __ldcg(pp + (1 * 128 + r) * BN + half * HB + j);
+          }
+          acc_g[j] = s0;
+          if constexpr (kG1) acc_u[j] = s1;
+        }
+      }
 
       if constexpr (kG1) {
-        // ---- SwiGLU + FP8 hi/lo quantisation of C, per 64-column block m ----
-        float* exh = ex + half * 64 * 33;  // [64 rows][33] (32 token columns + pad)
+        // ---- SwiGLU + FP8 hi/lo quantisation of C, per 128-column block m ----
+        // thread row r holds gate (x1) and up (x2) of C column 128 m + r
+        float* exh = ex + half * 128 * (CW + 1);  // [128 rows][CW + 1]
 #pragma unroll
         for (int sc = 0; sc < HB / CW; ++sc) {
           const int cbase = half * HB + sc * CW;
           if (cbase < ncols) {
-            if (q >= 2) {
 #pragma unroll
-              for (int i = 0; i < CW; ++i) exh[(r - 64) * 33 + i] = silu(acc[sc * CW + i]);
+            for (int i = 0; i < CW; ++i)
+              exh[r * (CW + 1) + i] = acc_g[sc * CW + i] * silu(acc_u[sc * CW + i]);
+            named_bar(bar_half, 128);
+            // 4 threads per token column, 32 C columns each
+            const int i = tid_h >> 2, p = tid_h & 3;
+            float vals[32];
+            float amax = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+              vals[k] = exh[(p * 32 + k) * (CW + 1) + (i < CW ? i : 0)];
+              amax = fmaxf(amax, fabsf(vals[k]));
             }
-            named_bar(bar_id, 128);
-            if (q < 2) {
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+            if (i < CW && cbase + i < ncols) {
+              const float inv = amax > 0.0f ? 448.0f / amax : 0.0f;
+              uint32_t hi[8], lo[8];
 #pragma unroll
-              for (int i = 0; i < CW; ++i) exh[r * 33 + i] *= acc[sc * CW + i];
-            }
-            named_bar(bar_id, 128);
-            if (q < 2) {
-              const int i = r >> 1, p = r & 1;  // token column i, C columns [32p, 32p+32)
-              float vals[32];
-              float amax = 0.0f;
+              for (int k = 0; k < 32; k += 4) {
+                float x[4], h[4], l[4];
 #pragma unroll
-              for (int k = 0; k < 32; ++k) {
-                vals[k] = exh[(p * 32 + k) * 33 + (i < CW ? i : 0)];
-                amax = fmaxf(amax, fabsf(vals[k]));
+                for (int u = 0; u < 4; ++u) x[u] = vals[k + u] * inv;
+                const __nv_fp8x2_storage_t h01 =
+                    __nv_cvt_float2_to_fp8x2(make_float2(x[0], x[1]), __NV_SATFINITE, __NV_E4M3);
+                const __nv_fp8x2_storage_t h23 =
+                    __nv_cvt_float2_to_fp8x2(make_float2(x[2], x[3]), __NV_SATFINITE, __NV_E4M3);
+                const __half2_raw hr01 = __nv_cvt_fp8x2_to_halfraw2(h01, __NV_E4M3);
+                const __half2_raw hr23 = __nv_cvt_fp8x2_to_halfraw2(h23, __NV_E4M3);
+                const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&hr01));
+                const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&hr23));
+                h[0] = f01.x; h[1] = f01.y; h[2] = f23.x; h[3] = f23.y;
+#pragma unroll
+                for (int u = 0; u < 4; ++u) l[u] = x[u] - h[u];
+                const __nv_fp8x2_storage_t l01 =
+                    __nv_cvt_float2_to_fp8x2(make_float2(l[0], l[1]), __NV_SATFINITE, __NV_E4M3);
+                const __nv_fp8x2_storage_t l23 =
+                    __nv_cvt_float2_to_fp8x2(make_float2(l[2], l[3]), __NV_SATFINITE, __NV_E4M3);
+                hi[k / 4] = (uint32_t)h01 | ((uint32_t)h23 << 16);
+                lo[k / 4] = (uint32_t)l01 | ((uint32_t)l23 << 16);
               }
-              amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-              if (i < CW && cbase + i < ncols) {
-                const float inv = amax > 0.0f ? 448.0f / amax : 0.0f;
-                uint32_t hi[8], lo[8];
-#pragma unroll
-                for (int k = 0; k < 32; k += 4) {
-                  float x[4], h[4], l[4];
-#pragma unroll
-                  for (int u = 0; u < 4; ++u) x[u] = vals[k + u] * inv;
-                  const __nv_fp8x2_storage_t h01 =
-                      __nv_cvt_float2_to_fp8x2(make_float2(x[0], x[1]), __NV_SATFINITE, __NV_E4M3);
-                  const __nv_fp8x2_storage_t h23 =
-                      __nv_cvt_float2_to_fp8x2(make_float2(x[2], x[3]), __NV_SATFINITE, __NV_E4M3);
-                  const __half2_raw hr01 = __nv_cvt_fp8x2_to_halfraw2(h01, __NV_E4M3);
-                  const __half2_raw hr23 = __nv_cvt_fp8x2_to_halfraw2(h23, __NV_E4M3);
-                  const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&hr01));
-                  const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&hr23));
-                  h[0] = f01.x; h[1] = f01.y; h[2] = f23.x; h[3] = f23.y;
-#pragma unroll
-                  for (int u = 0; u < 4; ++u) l[u] = x[u] - h[u];
-                  const __nv_fp8x2_storage_t l01 =
-                      __nv_cvt_float2_to_fp8x2(make_float2(l[0], l[1]), __NV_SATFINITE, __NV_E4M3);
-                  const __nv_fp8x2_storage_t l23 =
-                      __nv_cvt_float2_to_fp8x2(make_float2(l[2], l[3]), __NV_SATFINITE, __NV_E4M3);
-                  hi[k / 4] = (uint32_t)h01 | ((uint32_t)h23 << 16);
-                  lo[k / 4] = (uint32_t)l01 | ((uint32_t)l23 << 16);
-                }
-                const int64_t row = ch.row0 + cbase + i;
-                uint8_t* dst = args.cq + row * (2 * (int64_t)args.I) + m * 128 + p * 32;
-                reinterpret_cast<uint4*>(dst)[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                reinterpret_cast<uint4*>(dst)[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-                reinterpret_cast<uint4*>(dst + 64)[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                reinterpret_cast<uint4*>(dst + 64)[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
-                if (p == 0) args.c_scale[(int64_t)m * args.row_cap + row] = amax / 448.0f;
-              }
+              const int64_t row = ch.row0 + cbase + i;
+              uint8_t* dst = args.cq + row * (2 * (int64_t)args.I) + m * 256 + p * 32;
+              reinterpret_cast<uint4*>(dst)[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+              reinterpret_cast<uint4*>(dst)[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+              reinterpret_cast<uint4*>(dst + 128)[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+              reinterpret_cast<uint4*>(dst + 128)[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+              if (p == 0) args.c_scale[(int64_t)m * args.row_cap + row] = amax / 448.0f;
             }
-            named_bar(bar_id, 128);
+            named_bar(bar_half, 128);
           }
         }
       } else {
@@ -354,7 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (col < ch.rows) {
             const int64_t row = ch.row0 + col;
             const float w = __ldg(args.row_w + row);
-            args.ow[row * args.H + h] = __float2bfloat16_rn(acc[j] * w);
+            args.ow[row * args.H + h] = __float2bfloat16_rn(acc_g[j] * w);
           }
         }
       }
@@ -390,8 +492,12 @@ cudaError_t launch_one(const CUtensorMap& a, const CUtensorMap& b, const GemmArg
 
 }  // namespace
 
-bool gemm_bn_supported(int bn) {
-  return bn == 16 || bn == 32 || bn == 64 || bn == 128 || bn == 256;
+bool gemm_bn_supported(int bn) { return bn == 16 || bn == 32 || bn == 64; }
+
+size_t gemm_partial_bytes() {
+  // split-K is used only when tiles < 2 x SMs, so units < 4 x SMs; one partial tile is
+  // at most 2 accumulators x 128 rows x 64 columns of fp32 (GEMM1) or 128 x 64 (GEMM2)
+  return (size_t)4 * kMaxSms * 2 * 128 * 64 * sizeof(float);
 }
 
 cudaError_t launch_gemm1(int bn, const CUtensorMap& w13_map, const CUtensorMap& a_map,
@@ -400,8 +506,6 @@ cudaError_t launch_gemm1(int bn, const CUtensorMap& w13_map, const CUtensorMap& 
     case 16: return launch_one<16, true>(w13_map, a_map, args, grid, stream);
     case 32: return launch_one<32, true>(w13_map, a_map, args, grid, stream);
     case 64: return launch_one<64, true>(w13_map, a_map, args, grid, stream);
-    case 128: return launch_one<128, true>(w13_map, a_map, args, grid, stream);
-    case 256: return launch_one<256, true>(w13_map, a_map, args, grid, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -412,8 +516,6 @@ cudaError_t launch_gemm2(int bn, const CUtensorMap& w2_map, const CUtensorMap& c
     case 16: return launch_one<16, false>(w2_map, cq_map, args, grid, stream);
     case 32: return launch_one<32, false>(w2_map, cq_map, args, grid, stream);
     case 64: return launch_one<64, false>(w2_map, cq_map, args, grid, stream);
-    case 128: return launch_one<128, false>(w2_map, cq_map, args, grid, stream);
-    case 256: return launch_one<256, false>(w2_map, cq_map, args, grid, stream);
     default: return cudaErrorInvalidValue;
   }
 }

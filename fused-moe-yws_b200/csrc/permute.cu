@@ -68,10 +68,12 @@ __global__ void __launch_bounds__(256) scatter_gather_kernel(ScatterArgs a) {
       }
     }
     s_row[i] = row;
-    if (t < a.T) a.token_row[t * K + i % K] = row;
-    if (row >= 0) {
-      a.row_token[row] = (int)t;
-      a.row_w[row] = a.topk_w[t * K + i % K];
+    if (blockIdx.y == 0) {
+      if (t < a.T) a.token_row[t * K + i % K] = row;
+      if (row >= 0) {
+        a.row_token[row] = (int)t;
+        a.row_w[row] = a.topk_w[t * K + i % K];
+      }
     }
   }
   __syncthreads();
@@ -83,40 +85,48 @@ __global__ void __launch_bounds__(256) scatter_gather_kernel(ScatterArgs a) {
   }
   __syncthreads();
   const int n = s_nlocal;
+  // this CTA copies 16-byte column vectors [v0, v1) of every local row
   const int vpr = a.H / 16;
-  for (int v = tid; v < n * vpr; v += blockDim.x) {
-    const int li = v / vpr, part = v - li * vpr;
+  const int v0 = (int)((int64_t)vpr * blockIdx.y / gridDim.y);
+  const int v1 = (int)((int64_t)vpr * (blockIdx.y + 1) / gridDim.y);
+  const int vw = v1 - v0;
+  for (int v = tid; v < n * vw; v += blockDim.x) {
+    const int li = v / vw, part = v0 + (v - li * vw);
     const int i = s_list[li];
     const int64_t t = t0 + i / K;
     const uint4 x = ld_nc_v4(a.hidden + t * a.H + part * 16);
     *reinterpret_cast<uint4*>(a.a_perm + (int64_t)s_row[i] * a.H + part * 16) = x;
   }
   const int kb = a.H / kBlock;
-  for (int v = tid; v < n * kb; v += blockDim.x) {
-    const int li = v / kb, b = v - li * kb;
-    const int i = s_list[li];
-    const int64_t t = t0 + i / K;
-    a.a_scale[(int64_t)b * a.row_cap + s_row[i]] = a.hidden_scale[(int64_t)b * a.T + t];
+  if (blockIdx.y == 0) {
+    for (int v = tid; v < n * kb; v += blockDim.x) {
+      const int li = v / kb, b = v - li * kb;
+      const int i = s_list[li];
+      const int64_t t = t0 + i / K;
+      a.a_scale[(int64_t)b * a.row_cap + s_row[i]] = a.hidden_scale[(int64_t)b * a.T + t];
+    }
   }
-  // padding rows of the experts this CTA owns (expert e goes to CTA e % gridDim.x)
+  // padding rows of the experts this CTA column owns (expert e goes to x = e % gridDim.x)
   for (int e = blockIdx.x; e < a.E_local; e += gridDim.x) {
     const int cnt = a.expert_cnt[e];
     const int r0 = a.expert_off[e] + cnt;
     const int npad = (cnt + kRowAlign - 1) / kRowAlign * kRowAlign - cnt;
     const uint4 z = make_uint4(0, 0, 0, 0);
-    for (int v = tid; v < npad * vpr; v += blockDim.x) {
-      const int r = r0 + v / vpr;
+    for (int v = tid; v < npad * vw; v += blockDim.x) {
+      const int r = r0 + v / vw;
       if (r < a.row_cap)
-        *reinterpret_cast<uint4*>(a.a_perm + (int64_t)r * a.H + (v % vpr) * 16) = z;
+        *reinterpret_cast<uint4*>(a.a_perm + (int64_t)r * a.H + (v0 + v % vw) * 16) = z;
     }
-    for (int v = tid; v < npad * kb; v += blockDim.x) {
-      const int r = r0 + v / kb;
-      if (r < a.row_cap) a.a_scale[(int64_t)(v % kb) * a.row_cap + r] = 0.0f;
-    }
-    for (int v = tid; v < npad; v += blockDim.x) {
-      if (r0 + v < a.row_cap) {
-        a.row_token[r0 + v] = -1;
-        a.row_w[r0 + v] = 0.0f;
+    if (blockIdx.y == 0) {
+      for (int v = tid; v < npad * kb; v += blockDim.x) {
+        const int r = r0 + v / kb;
+        if (r < a.row_cap) a.a_scale[(int64_t)(v % kb) * a.row_cap + r] = 0.0f;
+      }
+      for (int v = tid; v < npad; v += blockDim.x) {
+        if (r0 + v < a.row_cap) {
+          a.row_token[r0 + v] = -1;
+          a.row_w[r0 + v] = 0.0f;
+        }
       }
     }
   }
@@ -127,8 +137,10 @@ __global__ void __launch_bounds__(128) combine_kernel(CombineArgs a) {
   const int64_t t = blockIdx.x;
   if (threadIdx.x < a.top_k) s_rows[threadIdx.x] = a.token_row[t * a.top_k + threadIdx.x];
   __syncthreads();
+  // this CTA covers 8-element vectors [blockIdx.y * 128, +128) of the token's row
   const int nv = a.H / 8;
-  for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+  const int vend = min(nv, (int)(blockIdx.y + 1) * 128);
+  for (int v = blockIdx.y * 128 + threadIdx.x; v < vend; v += blockDim.x) {
     float acc[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) acc[j] = 0.0f;

@@ -42,6 +42,17 @@ __device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
 
 }  // namespace
 
+// Order-preserving map of a float to uint32 (larger float -> larger key). Only used
+// for candidates, which are never NaN or -inf; key 0 therefore means "no candidate".
+__device__ __forceinline__ uint32_t order_key(float v) {
+  const uint32_t b = __float_as_uint(v);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+__device__ __forceinline__ float key_value(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+__device__ __forceinline__ bool is_candidate(float v) { return v > -INFINITY; }  // not NaN/-inf
+
 __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
   __shared__ float s_sc[kWarps][kMaxE];
   __shared__ float s_wb[kWarps][kMaxE];
@@ -55,12 +66,13 @@ __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int E = a.E, G = a.E / a.n_group, K = a.top_k;
+  const int EPL = (E + 31) / 32;  // experts per lane (lane owns lane + 32 j)
   for (int i = threadIdx.x; i < a.E_local; i += blockDim.x) s_cnt[i] = 0;
   __syncthreads();
 
   const int64_t t = (int64_t)blockIdx.x * kWarps + warp;
   if (t < a.T) {
-    // 1) sigmoid + bias into shared memory (strided, coalesced loads)
+    // 1) sigmoid + bias (strided, coalesced loads)
     const float* lrow = a.logits + t * E;
     for (int e = lane; e < E; e += 32) {
       const float sg = exact_sigmoid(__ldg(lrow + e));
@@ -68,8 +80,23 @@ __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
       s_wb[warp][e] = __fadd_rn(sg, bf16_bits_to_float(__ldg(a.bias + e)));
     }
     __syncwarp();
-    // 2) group scores: lane g scans its group exactly like the reference loop
-    if (lane < a.n_group) {
+    // 2) group scores = sum of the two largest biased scores (NaN and -inf never count,
+    //    exactly as the reference's strict '>' scan from -inf)
+    if (G == 32) {
+      // one expert of every group per lane: warp-wide top-2 per group via redux
+      for (int g = 0; g < a.n_group; ++g) {
+        const float v = s_wb[warp][g * 32 + lane];
+        const uint32_t k = is_candidate(v) ? order_key(v) : 0u;
+        const uint32_t k1 = __reduce_max_sync(0xffffffffu, k);
+        const unsigned dup = __popc(__ballot_sync(0xffffffffu, k == k1 && k1 != 0u));
+        const uint32_t k2 = dup >= 2 ? k1 : __reduce_max_sync(0xffffffffu, k == k1 ? 0u : k);
+        if (lane == 0) {
+          const float b0 = k1 ? key_value(k1) : -INFINITY;
+          const float b1 = k2 ? key_value(k2) : -INFINITY;
+          s_gscore[warp][g] = __fadd_rn(b0, b1);
+        }
+      }
+    } else if (lane < a.n_group) {
       float b0 = -INFINITY, b1 = -INFINITY;
       for (int j = 0; j < G; ++j) {
         const float v = s_wb[warp][lane * G + j];
@@ -96,50 +123,46 @@ __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
       }
     }
     keep = __shfl_sync(0xffffffffu, keep, 0);
-    // 4) top_k experts by warp-wide arg-max rounds; lane owns experts lane, lane+32, ...
-    uint32_t taken = 0;  // bit j: expert lane + 32 j already selected
+    // 4) top_k experts: per round a warp max of the order key, ties to the lowest id
+    uint32_t cand = 0;  // bit j: expert lane + 32 j is still a candidate
+    for (int j = 0; j < EPL; ++j) {
+      const int e = lane + 32 * j;
+      if (e < E && ((keep >> (e / G)) & 1u) && is_candidate(s_wb[warp][e])) cand |= 1u << j;
+    }
     int* sel = s_sel[warp];
     for (int k = 0; k < K; ++k) {
-      float bv = -INFINITY;
-      int bi = -1;
-      for (int j = 0; lane + 32 * j < E; ++j) {
+      uint32_t best_k = 0u;
+      int best_e = 0x7fffffff;
+      for (uint32_t c = cand; c; c &= c - 1) {
+        const int j = __ffs(c) - 1;
         const int e = lane + 32 * j;
-        if ((taken >> j) & 1u) continue;
-        if (!((keep >> (e / G)) & 1u)) continue;
-        const float v = s_wb[warp][e];
-        if (!(v > -INFINITY)) continue;  // NaN and -inf are never selected
-        if (bi < 0 || ranks_above(v, e, bv, bi)) {
-          bv = v;
-          bi = e;
+        const uint32_t key = order_key(s_wb[warp][e]);
+        if (key > best_k) {  // ascending j: ties keep the lower id
+          best_k = key;
+          best_e = e;
         }
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (oi >= 0 && (bi < 0 || ranks_above(ov, oi, bv, bi))) {
-          bv = ov;
-          bi = oi;
-        }
-      }
+      const uint32_t kmax = __reduce_max_sync(0xffffffffu, best_k);
+      const uint32_t win = __reduce_min_sync(0xffffffffu,
+                                             (best_k == kmax && kmax != 0u) ? (uint32_t)best_e
+                                                                            : 0xffffffffu);
+      const int bi = kmax != 0u ? (int)win : -1;
       if (lane == 0) sel[k] = bi;
-      if (bi >= 0 && (bi & 31) == lane) taken |= 1u << (bi >> 5);
+      if (bi >= 0 && (bi & 31) == lane) cand &= ~(1u << (bi >> 5));
     }
     __syncwarp();
     // 5) weights in selection order, local histogram
-    if (lane == 0) {
+    if (lane < K) {
+      // each lane needs the same left-to-right sum: compute it redundantly in order
       float sum = 0.0f;
       for (int k = 0; k < K; ++k)
         if (sel[k] >= 0) sum = __fadd_rn(sum, s_sc[warp][sel[k]]);
       sum = __fadd_rn(sum, 1e-20f);
-      for (int k = 0; k < K; ++k) {
-        const int e = sel[k];
-        a.topk_idx[t * K + k] = e;
-        a.topk_w[t * K + k] =
-            e >= 0 ? __fmul_rn(__fdiv_rn(s_sc[warp][e], sum), a.rsf) : 0.0f;
-        const int le = e - a.local_offset;
-        if (e >= 0 && le >= 0 && le < a.E_local) atomicAdd(&s_cnt[le], 1);
-      }
+      const int e = sel[lane];
+      a.topk_idx[t * K + lane] = e;
+      a.topk_w[t * K + lane] = e >= 0 ? __fmul_rn(__fdiv_rn(s_sc[warp][e], sum), a.rsf) : 0.0f;
+      const int le = e - a.local_offset;
+      if (e >= 0 && le >= 0 && le < a.E_local) atomicAdd(&s_cnt[le], 1);
     }
   }
   __syncthreads();
@@ -166,21 +189,41 @@ __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
     if (lane == 0) s_tot[e] = sum;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int off = 0, choff = 0;
-    for (int e = 0; e < a.E_local; ++e) {
-      s_off[e] = off;
-      s_choff[e] = choff;
-      off += (s_tot[e] + kRowAlign - 1) / kRowAlign * kRowAlign;
-      choff += (s_tot[e] + a.bn - 1) / a.bn;
+  if (warp == 0) {
+    // exclusive scans over experts (two experts per lane covers E_local <= 64)
+    int run_off = 0, run_ch = 0;
+    for (int base = 0; base < a.E_local; base += 32) {
+      const int e = base + lane;
+      const int tot = e < a.E_local ? s_tot[e] : 0;
+      const int pad = (tot + kRowAlign - 1) / kRowAlign * kRowAlign;
+      const int nch = (tot + a.bn - 1) >> a.bn_log2;
+      int io = pad, ic = nch;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int yo = __shfl_up_sync(0xffffffffu, io, o);
+        const int yc = __shfl_up_sync(0xffffffffu, ic, o);
+        if (lane >= o) {
+          io += yo;
+          ic += yc;
+        }
+      }
+      if (e < a.E_local) {
+        s_off[e] = run_off + io - pad;
+        s_choff[e] = run_ch + ic - nch;
+      }
+      run_off += __shfl_sync(0xffffffffu, io, 31);
+      run_ch += __shfl_sync(0xffffffffu, ic, 31);
     }
-    s_off[a.E_local] = off;
-    s_choff[a.E_local] = choff;
-    a.expert_off[a.E_local] = off;
-    a.meta[kMetaTotalRows] = off;
-    a.meta[kMetaNumChunks] = choff < a.max_chunks ? choff : (int)a.max_chunks;
-    if (off > a.row_cap || choff > a.max_chunks) atomicOr(a.meta + kMetaError, kErrRowOverflow);
-    a.meta[kMetaTicket] = 0;  // ready for the next launch on this workspace
+    if (lane == 0) {
+      s_off[a.E_local] = run_off;
+      s_choff[a.E_local] = run_ch;
+      a.expert_off[a.E_local] = run_off;
+      a.meta[kMetaTotalRows] = run_off;
+      a.meta[kMetaNumChunks] = run_ch < a.max_chunks ? run_ch : (int)a.max_chunks;
+      if (run_off > a.row_cap || run_ch > a.max_chunks)
+        atomicOr(a.meta + kMetaError, kErrRowOverflow);
+      a.meta[kMetaTicket] = 0;  // ready for the next launch on this workspace
+    }
   }
   __syncthreads();
   for (int e = threadIdx.x; e < a.E_local; e += blockDim.x) {
@@ -192,7 +235,7 @@ __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
       Chunk ch;
       ch.expert = e;
       ch.row0 = s_off[e] + r;
-      ch.rows = min(a.bn, n - r);
+      ch.rows = n - r < a.bn ? n - r : a.bn;
       ch.ncols = (ch.rows + kRowAlign - 1) / kRowAlign * kRowAlign;
       a.chunks[s_choff[e] + c] = ch;
     }

@@ -88,6 +88,17 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 1D bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16),
+// completion signalled on `bar` (complete_tx).
+__device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes,
+                                             uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
 // L2 eviction-priority policies for the cache_hint operand.
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;

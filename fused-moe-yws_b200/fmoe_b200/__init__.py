@@ -311,6 +311,8 @@ class StageTimer:
 
     def __init__(self):
         self.events = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+        for e in self.events:  # torch creates the CUDA event lazily, on first record
+            e.record()
         self._arr = (ctypes.c_void_p * 6)(*[e.cuda_event for e in self.events])
 
     def __enter__(self):

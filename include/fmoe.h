@@ -44,8 +44,8 @@ typedef struct fmoe_problem {
   int64_t num_tokens;          /* T: routing_logits.shape[0] */
   int32_t num_experts;         /* E_global: routing_logits.shape[1] (<= 256, multiple of n_group) */
   int32_t num_local_experts;   /* E_local: gemm1_weights.shape[0] (<= 64) */
-  int32_t hidden_size;         /* H: multiple of 128 */
-  int32_t intermediate_size;   /* I: multiple of 128 */
+  int32_t hidden_size;         /* H: multiple of 128, <= 16384 */
+  int32_t intermediate_size;   /* I: multiple of 128, <= 16384 */
   int32_t top_k;               /* experts per token (<= 32) */
   int32_t n_group;             /* routing groups (<= 32) */
   int32_t topk_group;          /* groups kept per token */
