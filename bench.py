@@ -172,6 +172,38 @@ def time_device(inp, steps, warmup, flush, stage=False):
     return ms, stages, out
 
 
+def time_graph(inp, steps, warmup, flush):
+    """Per-call device time (ms) of the operator replayed from a CUDA graph (all five
+    kernels and the workspace memset captured once); L2 flushed between replays."""
+    args = W.operator_args(inp)
+    out = torch.empty(args[0].shape[0], 7168, dtype=torch.bfloat16, device="cuda")
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(warmup):
+            fmoe_b200.kernel(*args, 0, 2.5, out=out)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fmoe_b200.kernel(*args, 0, 2.5, out=out)
+    for _ in range(warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    pairs = []
+    for _ in range(steps):
+        flush.zero_()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        graph.replay()
+        e1.record()
+        pairs.append((e0, e1))
+    torch.cuda.synchronize()
+    ms = [a.elapsed_time(b) for a, b in pairs]
+    del graph
+    return ms, out
+
+
 def time_e2e(inp, steps, warmup):
     """Public API with host buffers: H2D of the activations and D2H of the output inside."""
     names = ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")
@@ -229,12 +261,14 @@ def sweep(seed, hbm_peak, fp8_peak):
                          ("config2", 4096, 0), ("config2", 8192, 0), ("config4", 4096, 8)]:
         inp = make_workload(T, seed, skew)
         rows, active = routed_stats(inp)
-        ms, stages, _ = time_device(inp, steps=10, warmup=3, flush=flush, stage=True)
+        ms_e, stages, _ = time_device(inp, steps=10, warmup=3, flush=flush, stage=True)
+        ms, _ = time_graph(inp, steps=10, warmup=3, flush=flush)
         t = statistics.median(ms)
         st = [statistics.median(s[i] for s in stages) for i in range(5)]
         b = layer_bytes(T, active)
         res.append({"config": cfg, "T": T, "skew_hot": skew, "rows": rows,
                     "active_experts": active, "us_per_call": round(t * 1e3, 1),
+                    "us_per_call_eager": round(statistics.median(ms_e) * 1e3, 1),
                     "tokens_per_s": round(T / (t * 1e-3), 1),
                     "hbm_gbs": round(b / (t * 1e-3) / 1e9, 1),
                     "hbm_frac": round(b / (t * 1e-3) / 1e9 / hbm_peak, 3),
@@ -337,8 +371,13 @@ def main():
     torch.cuda.synchronize()
     gpu_index = int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local]) \
         if os.environ.get("CUDA_VISIBLE_DEVICES") else local
+    # eager pass with stage events (per-kernel durations for the roofline)
+    ms_eager, stages, _ = time_device(inp, args.steps, args.warmup, flush, stage=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
     with ClockSampler(gpu_index) as clk:
-        ms, stages, _ = time_device(inp, args.steps, args.warmup, flush, stage=True)
+        ms, _ = time_graph(inp, args.steps, args.warmup, flush)
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
@@ -378,6 +417,7 @@ def main():
         "metric": "MoE layer tokens/s (DS-V3 decode, T=64)", "value": round(value, 1),
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_per_step, 4), "us_per_call": round(ms_per_step * 1e3, 1),
+        "us_per_call_eager": round(statistics.mean(ms_eager) * 1e3, 1),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "e4m3 x e4m3 -> fp32 (tcgen05 kind::f8f6f4), fp32 block-scale promotion",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, FP8 128-block scales)",
@@ -386,7 +426,8 @@ def main():
                    "top_k": 8, "n_group": 8, "topk_group": 4, "routed_rows": rows,
                    "active_experts": active, "tile_n": fmoe_b200.load_library()
                    .fmoe_autotune_tile_n(T), "parallelism": f"replicas x{world}",
-                   "l2": "flushed between calls (256 MiB write); weights 1.2 GB > L2"},
+                   "l2": "flushed between calls (256 MiB write); weights 1.2 GB > L2",
+                   "launch": "one CUDA graph replay per step (memset + 5 PDL kernels)"},
         "roofline": roofline, "clocks": clocks, "e2e": e2e,
         "gpu_launches": 5 * args.steps,
     }

@@ -201,8 +201,8 @@ int launch_route(const fmoe_problem* p, const Carved& c, const float* logits, co
   FMOE_CUDA_TRY(cudaMemsetAsync(c.at<int>(c.L.meta), 0, c.L.counters - c.L.meta +
                                 kTileCounters * sizeof(int), stream));
   const RouteArgs ra = route_args(p, c, logits, bias, bn);
-  route_plan_kernel<<<(unsigned)c.L.n_route_ctas, kRouteTokensPerCta * 32, 0, stream>>>(ra);
-  FMOE_CUDA_TRY(cudaGetLastError());
+  FMOE_CUDA_TRY(launch_pdl(route_plan_kernel, dim3((unsigned)c.L.n_route_ctas),
+                           dim3(kRouteTokensPerCta * 32), 0, stream, ra));
   return FMOE_OK;
 }
 
@@ -282,9 +282,10 @@ extern "C" int fmoe_forward(const fmoe_problem* p, const fmoe_tensors* t, void* 
     const int sms = num_sms_current();
     int parts = (int)((2 * sms + c.L.n_route_ctas - 1) / c.L.n_route_ctas);
     parts = parts < 1 ? 1 : (parts > 28 ? 28 : parts);
-    scatter_gather_kernel<<<dim3((unsigned)c.L.n_route_ctas, (unsigned)parts), 256, 0, stream>>>(sa);
+    FMOE_CUDA_TRY(launch_pdl(scatter_gather_kernel,
+                             dim3((unsigned)c.L.n_route_ctas, (unsigned)parts), dim3(256), 0,
+                             stream, sa));
   }
-  FMOE_CUDA_TRY(cudaGetLastError());
   if ((v = mark_stage(2, stream)) != FMOE_OK) return v;
 
   CUtensorMap m_w13, m_a, m_w2, m_cq;
@@ -340,8 +341,8 @@ extern "C" int fmoe_forward(const fmoe_problem* p, const fmoe_tensors* t, void* 
   ca.T = T;
   ca.H = H;
   ca.top_k = p->top_k;
-  combine_kernel<<<dim3((unsigned)T, (unsigned)((H / 8 + 127) / 128)), 128, 0, stream>>>(ca);
-  FMOE_CUDA_TRY(cudaGetLastError());
+  FMOE_CUDA_TRY(launch_pdl(combine_kernel, dim3((unsigned)T, (unsigned)((H / 8 + 127) / 128)),
+                           dim3(128), 0, stream, ca));
   return mark_stage(5, stream);
 }
 

@@ -102,6 +102,17 @@ inline WorkspaceLayout make_layout(const Geometry& g) {
   return L;
 }
 
+// ----------------------------------------------------------------------------- PDL
+// Programmatic dependent launch: every kernel of the operator is launched with
+// programmatic stream serialization. pdl_wait() blocks until the preceding kernel in
+// the stream has completed and its writes are visible; it must come before the first
+// global-memory access to the workspace. pdl_trigger() lets the next kernel start
+// launching (its CTAs then run their own prologue and wait in pdl_wait()).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ----------------------------------------------------------------------------- sigmoid
 // exp(x) by Cody-Waite reduction (ln2 = hi + lo), a degree-7 Taylor polynomial on
 // |r| <= ln2/2 and an exact two-step scaling by 2^n. Only IEEE round-to-nearest

@@ -115,6 +115,59 @@ __device__ __forceinline__ void promote(float (&acc)[HB], uint32_t taddr, const 
   }
 }
 
+// Store HB floats (16-byte aligned) as float4 vectors.
+template <int HB>
+__device__ __forceinline__ void store_row(float* dst, const float (&v)[HB]) {
+  if constexpr (HB % 4 == 0) {
+#pragma unroll
+    for (int j = 0; j < HB; j += 4)
+      *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < HB; ++j) dst[j] = v[j];
+  }
+}
+
+// acc = sum over splits s = 0..n-1 of partial_s, in split order; split `own` comes from
+// the registers. Loads of all other splits are issued before the first add so their
+// latencies overlap. Split-K partials come from other CTAs: L2-coherent loads.
+template <int HB, int kRegs>
+__device__ __forceinline__ void sum_partials(float (&acc)[HB], const float* src, int n, int own,
+                                             int stride) {
+  float out[HB];
+#pragma unroll
+  for (int j = 0; j < HB; ++j) out[j] = 0.0f;
+  constexpr int kBatch = kRegs / HB > 0 ? kRegs / HB : 1;  // splits in flight
+  for (int s0 = 0; s0 < n; s0 += kBatch) {
+    float buf[kBatch][HB];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int s = s0 + u;
+      if (s < n && s != own) {
+        const float* p = src + (int64_t)s * stride;
+#pragma unroll
+        for (int j = 0; j < HB; j += 4) {
+          const float4 x = __ldcg(reinterpret_cast<const float4*>(p + j));
+          buf[u][j] = x.x;
+          buf[u][j + 1] = x.y;
+          buf[u][j + 2] = x.z;
+          buf[u][j + 3] = x.w;
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int s = s0 + u;
+      if (s < n) {
+#pragma unroll
+        for (int j = 0; j < HB; ++j) out[j] += (s == own) ? acc[j] : buf[u][j];
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < HB; ++j) acc[j] = out[j];
+}
+
 template <int BN, bool kG1>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA,
@@ -172,6 +225,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();     // the permute / GEMM1 outputs of the previous kernel are now visible
+  pdl_trigger();  // let the next kernel's CTAs start their prologue as SMs free up
 
   const int num_tiles = args.meta[kMetaNumChunks] * args.m_tiles;
   const int KS = args.k_steps;
@@ -353,13 +408,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // ---- split-K: publish this unit's partial; the last unit of the tile finishes ----
       if (SPLIT > 1) {
+        // partial layout: [acc][row r][BN] floats; each thread owns HB contiguous floats
         float* part = args.partials + (int64_t)unit * C::kPartialFloats;
-#pragma unroll
-        for (int j = 0; j < HB; ++j) part[(0 * 128 + r) * BN + half * HB + j] = acc_g[j];
-        if constexpr (kG1) {
-#pragma unroll
-          for (int j = 0; j < HB; ++j) part[(1 * 128 + r) * BN + half * HB + j] = acc_u[j];
-        }
+        store_row<HB>(part + (0 * 128 + r) * BN + half * HB, acc_g);
+        if constexpr (kG1) store_row<HB>(part + (1 * 128 + r) * BN + half * HB, acc_u);
         __threadfence();
         named_bar(kBarAll, kEpiThreads);
         if (tid_e == 0) {
@@ -371,20 +423,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_bar(kBarAll, kEpiThreads);
         if (!*last_flag) continue;
         __threadfence();
-        // deterministic: sum the partials in split order
+        // deterministic: sum the partials in split order (all loads issued first)
         const float* base = args.partials + (int64_t)(tile * SPLIT) * C::kPartialFloats;
-#pragma unroll
-        for (int j = 0; j < HB; ++j) {
-          float s0 = 0.0f, s1 = 0.0f;
-          for (int s2 = 0; s2 < SPLIT; ++s2) {
-            const float* pp = base + (int64_t)s2 * C::kPartialFloats;
-            s0 += (s2 == sp) ? acc_g[j] : __ldcg(pp + (0 * 128 + r) * BN + half * HB + j);
-            if constexpr (kG1)
-              s1 += (s2 == sp) ? acc_u[j] : __ldcg(pp + (1 * 128 + r) * BN + half * HB + j);
-          }
-          acc_g[j] = s0;
-          if constexpr (kG1) acc_u[j] = s1;
-        }
+        constexpr int kRegs = kG1 ? 32 : 64;  // GEMM1 holds two accumulators
+        sum_partials<HB, kRegs>(acc_g, base + (0 * 128 + r) * BN + half * HB, SPLIT, sp,
+                                C::kPartialFloats);
+        if constexpr (kG1)
+          sum_partials<HB, kRegs>(acc_u, base + (1 * 128 + r) * BN + half * HB, SPLIT, sp,
+                                  C::kPartialFloats);
       }
 
       if constexpr (kG1) {
@@ -486,8 +532,7 @@ cudaError_t launch_one(const CUtensorMap& a, const CUtensorMap& b, const GemmArg
     if (e != cudaSuccess) return e;
     configured_device = dev;
   }
-  fn<<<grid, kThreads, C::kSmemBytes, stream>>>(a, b, args);
-  return cudaGetLastError();
+  return launch_pdl(fn, dim3(grid), dim3(kThreads), C::kSmemBytes, stream, a, b, args);
 }
 
 }  // namespace

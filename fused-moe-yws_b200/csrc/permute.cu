@@ -41,6 +41,8 @@ __global__ void __launch_bounds__(256) scatter_gather_kernel(ScatterArgs a) {
   const int tid = threadIdx.x;
   const int K = a.top_k, nent = kTok * K;
   const int64_t t0 = (int64_t)blockIdx.x * kTok;
+  pdl_wait();
+  pdl_trigger();
   for (int e = tid; e < a.E_local; e += blockDim.x)
     s_base[e] = a.cta_base[(int64_t)blockIdx.x * a.E_local + e];
   for (int i = tid; i < nent; i += blockDim.x) {
@@ -135,6 +137,8 @@ __global__ void __launch_bounds__(256) scatter_gather_kernel(ScatterArgs a) {
 __global__ void __launch_bounds__(128) combine_kernel(CombineArgs a) {
   __shared__ int s_rows[32];
   const int64_t t = blockIdx.x;
+  pdl_wait();
+  pdl_trigger();
   if (threadIdx.x < a.top_k) s_rows[threadIdx.x] = a.token_row[t * a.top_k + threadIdx.x];
   __syncthreads();
   // this CTA covers 8-element vectors [blockIdx.y * 128, +128) of the token's row

@@ -68,6 +68,8 @@ __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
   const int E = a.E, G = a.E / a.n_group, K = a.top_k;
   const int EPL = (E + 31) / 32;  // experts per lane (lane owns lane + 32 j)
   for (int i = threadIdx.x; i < a.E_local; i += blockDim.x) s_cnt[i] = 0;
+  pdl_wait();
+  pdl_trigger();
   __syncthreads();
 
   const int64_t t = (int64_t)blockIdx.x * kWarps + warp;
