@@ -47,7 +47,7 @@ from fmoe_b200 import workloads as W  # noqa: E402
 FLOP_PER_ROW = 88_080_384          # 2*H*2I + 2*I*H for DS-V3
 BYTES_PER_EXPERT = 44_050_944      # W13 + W2 FP8 + their fp32 block scales
 GEMM1_BYTES_PER_EXPERT = 29_360_128 + 32 * 56 * 4
-GEMM1_BYTES_PER_ROW = 7168 + 56 * 4 + 2 * 2048 + 32 * 4
+GEMM1_BYTES_PER_ROW = 7168 + 56 * 4 + 2 * 2048 + 16 * 4
 L2_FLUSH_BYTES = 256 << 20
 
 

@@ -264,3 +264,28 @@ def test_matches_reference_kernel(fmoe, ref_kernel, T):
     ref_out = torch.from_dlpack(ref_kernel(*W.operator_args(gpu), 0, 2.5))
     out = _run(fmoe, geo, gpu, 0, 2.5)
     _check(out, ref_out)
+
+
+@pytest.mark.parametrize("T", [1, 64, 2048])
+def test_cuda_graph_replay_matches_eager(fmoe, T):
+    """The operator is capturable (no host sync, no allocation inside the call) and a
+    graph replay (memset + five PDL-linked kernels) gives the eager result bit for bit."""
+    geo = W.DSV3
+    gpu, _, _ = _inputs(geo, T, seed=2)
+    args = W.operator_args(gpu)
+    ref = _run(fmoe, geo, gpu, 0, 2.5)
+    out = torch.empty_like(ref)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        fmoe.kernel(*args, 0, 2.5, out=out)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fmoe.kernel(*args, 0, 2.5, out=out)
+    out.zero_()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out.view(torch.int16), ref.view(torch.int16))
+    del graph
