@@ -8,7 +8,7 @@ generators are deterministic), and only the local experts the oracle routes to r
 weights; the other experts are zero and unread.
 
 Usage (on a GPU box, from the repository root):
-    python tests/golden/make_ref_goldens.py
+    python tests/golden/make_ref_goldens.py [--out-dir DIR]
 
 `tests/test_golden_cpu.py` checks the CPU oracle against these fixtures.
 """
@@ -48,7 +48,14 @@ def case_inputs(T, seed, ties, device="cpu"):
 
 
 def main():
+    import argparse
+
     import tvm_ffi
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--out-dir", default=str(Path(__file__).parent))
+    out_dir = Path(ap.parse_args().out_dir)
+    out_dir.mkdir(parents=True, exist_ok=True)
 
     so = ROOT / "oracle" / "_ref" / "ref_kernel.so"
     kern = tvm_ffi.load_module(str(so))["kernel"]
@@ -56,7 +63,7 @@ def main():
         inp, experts = case_inputs(T, seed, ties, device="cuda")
         out = torch.from_dlpack(kern(*W.operator_args(inp), 0, 2.5))
         torch.cuda.synchronize()
-        np.savez_compressed(Path(__file__).parent / f"{name}.npz",
+        np.savez_compressed(out_dir / f"{name}.npz",
                             out_bf16_bits=out.cpu().view(torch.int16).numpy(),
                             tokens=T, seed=seed, ties=ties, experts=np.array(experts),
                             local_expert_offset=0, routed_scaling_factor=2.5)
