@@ -209,6 +209,8 @@ int launch_route(const fmoe_problem* p, const Carved& c, const float* logits, co
 }  // namespace
 }  // namespace fmoe
 
+void fmoe::set_last_error(const std::string& msg) { g_last_error = msg; }
+
 using namespace fmoe;
 
 extern "C" int fmoe_abi_version(void) { return FMOE_ABI_VERSION; }

@@ -5,6 +5,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <string>
 #include <utility>
 
 #include "fmoe_common.cuh"
@@ -104,6 +105,7 @@ cudaError_t launch_gemm1(int bn, const CUtensorMap& w13_map, const CUtensorMap& 
 cudaError_t launch_gemm2(int bn, const CUtensorMap& w2_map, const CUtensorMap& cq_map,
                          const GemmArgs& args, int grid, cudaStream_t stream);
 bool gemm_bn_supported(int bn);
+void set_last_error(const std::string& msg);  // message returned by fmoe_last_error()
 size_t gemm_partial_bytes();
 
 }  // namespace fmoe

@@ -31,7 +31,7 @@ FMOE_OK, FMOE_ERR_VALUE, FMOE_ERR_TYPE, FMOE_ERR_RUNTIME, FMOE_ERR_WORKSPACE, FM
 
 EXPORTED_SYMBOLS = ("fmoe_abi_version", "fmoe_last_error", "fmoe_validate", "fmoe_workspace_size",
                     "fmoe_autotune_tile_n", "fmoe_forward", "fmoe_route", "fmoe_read_device_error",
-                    "fmoe_plan_view_get", "fmoe_set_stage_events")
+                    "fmoe_plan_view_get", "fmoe_set_stage_events", "fmoe_route_static")
 
 
 class FmoeProblem(ctypes.Structure):

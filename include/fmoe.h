@@ -133,6 +133,19 @@ typedef struct fmoe_plan_view {
 } fmoe_plan_view;
 int fmoe_plan_view_get(const fmoe_problem* p, void* workspace, fmoe_plan_view* view);
 
+/* Routing that takes no workspace and allocates nothing. This entry point has no
+ * counterpart in the reference operator. It exists for callers that cannot hand the
+ * library scratch memory: plugin interfaces that pass only the call's tensors, or engines
+ * that reserve all device memory at start-up and forbid later allocation (cudaMalloc would
+ * also synchronise the device and break stream capture). It computes what fmoe_route()
+ * computes, with its scratch in a fixed device array of about 0.53 MB per GPU that stays
+ * allocated until the process exits. Limits: num_tokens <= 8192, num_local_experts <= 64,
+ * top_k <= 32; larger problems fail with FMOE_ERR_VALUE. The first call on a device looks up
+ * the array's address there, so make it before any stream capture. All calls share the
+ * array: calls that overlap on the GPU race and must be ordered by the caller. */
+int fmoe_route_static(const fmoe_problem* p, const float* routing_logits,
+                      const void* routing_bias, const fmoe_route_out* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
