@@ -33,8 +33,7 @@ constexpr int kRowAlign = 16;      // expert row segments padded to the MMA N gr
 constexpr int kRouteTokensPerCta = 16;  // one warp per token in the routing kernel
 constexpr int kMaxBN = 64;         // largest token tile (MMA N) the GEMMs use
 constexpr int kMaxSms = 160;       // upper bound on SMs per GPU for split-K scratch sizing
-constexpr int kMaxSplit = 8;       // split-K factor cap
-constexpr int kTileCounters = 4 * kMaxSms;  // split-K arrival counters (tiles < 2 x SMs)
+constexpr int kTileCounters = kMaxSms;  // stream-K arrival counters, one per CTA
 
 struct Geometry {
   int64_t T;          // tokens
@@ -97,7 +96,7 @@ inline WorkspaceLayout make_layout(const Geometry& g) {
   L.cq = take((size_t)L.row_cap * 2 * g.I);
   L.c_scale = take((size_t)(g.I / kBlock) * L.row_cap * 4);
   L.ow = take((size_t)L.row_cap * g.H * 2);
-  L.partials = take((size_t)4 * kMaxSms * 2 * 128 * kMaxBN * 4);
+  L.partials = take((size_t)2 * kMaxSms * 2 * 128 * kMaxBN * 4);  // 2 slots per CTA
   L.total = off;
   return L;
 }

@@ -66,8 +66,8 @@ struct GemmArgs {
   const float* row_w;      // [row_cap]
   __nv_bfloat16* ow;       // [row_cap, H] weighted expert outputs
   int* err;                // device error word
-  float* partials;         // split-K partial tiles
-  int* tile_counters;      // split-K arrival counters (self-resetting, zeroed per call)
+  float* partials;         // stream-K partial tiles, [CTA][2 slots]
+  int* tile_counters;      // stream-K arrival counters by first contributor CTA (self-resetting)
 };
 
 struct CombineArgs {

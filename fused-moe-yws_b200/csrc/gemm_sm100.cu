@@ -54,12 +54,15 @@ struct Cfg {
   static constexpr int kBBytes = (kG1 ? 1 : 2) * BN * 128;   // tokens (G2: hi and lo)
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int HB = BN / 2;                           // token columns per half
-  static constexpr int CW = HB < 32 ? HB : 32;                // TMEM load width
+  // TMEM load width; GEMM1 keeps two accumulators live, so it loads narrower chunks
+  static constexpr int kCWMax = kG1 ? 16 : 32;
+  static constexpr int CW = HB < kCWMax ? HB : kCWMax;
   static constexpr int kBNs = BN < 32 ? 32 : BN;              // TMEM column stride
   static constexpr int kBufCols = kAcc * kBNs;
   static constexpr int kNBufRaw = 512 / kBufCols;
   static constexpr int kNBuf = kNBufRaw > 8 ? 8 : kNBufRaw;   // accumulator ring depth
-  static constexpr int kExBytes = kG1 ? 2 * 128 * (CW + 1) * 4 : 0;  // SwiGLU staging
+  static constexpr int kExBytes = kG1 ? 2 * 128 * (HB + 1) * 4 : 0;  // SwiGLU staging
+  static_assert(!kG1 || HB * 4 <= 128, "SwiGLU quantisation maps 4 threads per token column");
   static constexpr int kWscBytes = 2 * kMaxKSteps * 4;        // [gate/up][k step]
   static constexpr int kSlotBytes = BN * 4;                   // act scales of one K step
   static constexpr int kMaxSlots = 16 + 8 + 2;
@@ -87,15 +90,62 @@ __device__ __forceinline__ void set_error(int* err, volatile int* abort_flag, in
   *abort_flag = 1;
 }
 
-// Split-K factor for this launch: enough work units to cover every SM about twice
-// when the tile count alone cannot; identical in every CTA and role.
-__device__ __forceinline__ int split_factor(int num_tiles, int ks_total) {
-  if (num_tiles <= 0) return 1;
-  int s = (2 * (int)gridDim.x + num_tiles - 1) / num_tiles;
-  s = s < 1 ? 1 : s;
-  s = s > kMaxSplit ? kMaxSplit : s;
-  return s > ks_total ? ks_total : s;
-}
+// Stream-K work split: the launch's work is num_tiles x KS K-steps, CTA c owns the
+// contiguous global step range [start(c), start(c+1)). Ranges are cut at tile boundaries
+// into segments; a segment that does not cover its whole tile is a partial.
+struct StreamK {
+  int64_t W;  // total K-steps
+  int G;      // CTAs
+  __device__ __forceinline__ int64_t start(int c) const { return (int64_t)c * W / G; }
+  // the CTA whose range contains global step g
+  __device__ __forceinline__ int cta_of(int64_t g) const {
+    return (int)(((g + 1) * G + W - 1) / W) - 1;
+  }
+};
+
+// Per-CTA work sequence: whole tiles round-robin over the CTAs for all but the last one
+// to two waves ("data parallel": CTAs that run together work on neighbouring tiles, so an
+// expert's weight tiles are shared through L2 by its chunks), then the remaining tiles
+// split by stream-K so every CTA ends at the same time. Every role walks the same sequence.
+struct Schedule {
+  int KS, G, cta;
+  int dp_tiles;  // whole-tile prefix, a multiple of G
+  StreamK sk;    // over the remaining tiles, in K-step units
+  int64_t g, g_end;
+  int dp_next;
+
+  __device__ __forceinline__ Schedule(int num_tiles, int ks, int grid, int c) {
+    KS = ks;
+    G = grid;
+    cta = c;
+    dp_tiles = num_tiles > 2 * G ? (num_tiles / G - 1) * G : 0;
+    sk.W = (int64_t)(num_tiles - dp_tiles) * KS;
+    sk.G = G;
+    g = sk.start(c);
+    g_end = sk.start(c + 1);
+    dp_next = c;
+  }
+  // next segment: tile index, K-step range [k0, k1); false when done
+  __device__ __forceinline__ bool next(int& tile, int& k0, int& k1) {
+    if (dp_next < dp_tiles) {
+      tile = dp_next;
+      k0 = 0;
+      k1 = KS;
+      dp_next += G;
+      return true;
+    }
+    if (g < g_end) {
+      const int64_t lt = g / KS;
+      k0 = (int)(g % KS);
+      k1 = (int)((int64_t)KS < k0 + (g_end - g) ? KS : k0 + (g_end - g));
+      g += k1 - k0;
+      tile = dp_tiles + (int)lt;
+      return true;
+    }
+    return false;
+  }
+  __device__ __forceinline__ int64_t sk_begin() const { return sk.start(cta); }
+};
 
 // Promote one accumulator: acc[j] += D[row, col_j] * scale_j * sw for this thread's
 // half of the token columns (only column chunks below ncols are read).
@@ -128,23 +178,29 @@ __device__ __forceinline__ void store_row(float* dst, const float (&v)[HB]) {
   }
 }
 
-// acc = sum over splits s = 0..n-1 of partial_s, in split order; split `own` comes from
-// the registers. Loads of all other splits are issued before the first add so their
-// latencies overlap. Split-K partials come from other CTAs: L2-coherent loads.
+// acc = sum of the tile's contributions in K order (contributor CTAs cf..cl, each of
+// which -- this one included -- has stored its partial before the arrival counter).
+// A contributor's partial lives in slot 0 (its range starts inside the tile) or slot 1
+// (the tile ends its range); CTAs with an empty range contribute nothing. A batch of
+// contributors is loaded before the adds. The order is fixed, so the result does not
+// depend on which CTA finishes the tile. Partials come from other CTAs: L2-coherent loads.
 template <int HB, int kRegs>
-__device__ __forceinline__ void sum_partials(float (&acc)[HB], const float* src, int n, int own,
-                                             int stride) {
+__device__ __forceinline__ void sum_contributions(float (&acc)[HB], const float* partials,
+                                                  int64_t elem_off, int stride,
+                                                  const StreamK& sk, int64_t tile_begin, int cf,
+                                                  int cl) {
   float out[HB];
 #pragma unroll
   for (int j = 0; j < HB; ++j) out[j] = 0.0f;
-  constexpr int kBatch = kRegs / HB > 0 ? kRegs / HB : 1;  // splits in flight
-  for (int s0 = 0; s0 < n; s0 += kBatch) {
+  constexpr int kBatch = kRegs / HB > 0 ? kRegs / HB : 1;  // contributors in flight
+  for (int c0 = cf; c0 <= cl; c0 += kBatch) {
     float buf[kBatch][HB];
 #pragma unroll
     for (int u = 0; u < kBatch; ++u) {
-      const int s = s0 + u;
-      if (s < n && s != own) {
-        const float* p = src + (int64_t)s * stride;
+      const int c = c0 + u;
+      if (c <= cl && sk.start(c) != sk.start(c + 1)) {
+        const int slot = sk.start(c) >= tile_begin ? 0 : 1;
+        const float* p = partials + (int64_t)(2 * c + slot) * stride + elem_off;
 #pragma unroll
         for (int j = 0; j < HB; j += 4) {
           const float4 x = __ldcg(reinterpret_cast<const float4*>(p + j));
@@ -157,10 +213,10 @@ __device__ __forceinline__ void sum_partials(float (&acc)[HB], const float* src,
     }
 #pragma unroll
     for (int u = 0; u < kBatch; ++u) {
-      const int s = s0 + u;
-      if (s < n) {
+      const int c = c0 + u;
+      if (c <= cl && sk.start(c) != sk.start(c + 1)) {
 #pragma unroll
-        for (int j = 0; j < HB; ++j) out[j] += (s == own) ? acc[j] : buf[u][j];
+        for (int j = 0; j < HB; ++j) out[j] += buf[u][j];
       }
     }
   }
@@ -230,8 +286,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int num_tiles = args.meta[kMetaNumChunks] * args.m_tiles;
   const int KS = args.k_steps;
-  const int SPLIT = split_factor(num_tiles, KS);
-  const int num_units = num_tiles * SPLIT;
+  const int cta = (int)blockIdx.x;
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
@@ -240,11 +295,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint64_t pol_a = policy_evict_last();   // token tiles: re-read by every m tile
       int it = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
-        const int tile = unit / SPLIT, sp = unit % SPLIT;
+      Schedule sched(num_tiles, KS, (int)gridDim.x, cta);
+      int tile, k0, k1;
+      while (ok && sched.next(tile, k0, k1)) {
         const Chunk ch = args.chunks[tile / args.m_tiles];
         const int m = tile % args.m_tiles;
-        const int k0 = KS * sp / SPLIT, k1 = KS * (sp + 1) / SPLIT;
         const float* asrc = args.act_scale + ch.row0;
         for (int ks = k0; ks < k1; ++ks, ++it) {
           const int s = it % S, slot = it % SR;
@@ -287,11 +342,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       int it = 0;
       bool ok = true;
-      for (int unit = blockIdx.x; unit < num_units && ok; unit += gridDim.x) {
-        const int tile = unit / SPLIT, sp = unit % SPLIT;
+      Schedule sched(num_tiles, KS, (int)gridDim.x, cta);
+      int tile, k0, k1;
+      while (ok && sched.next(tile, k0, k1)) {
         const Chunk ch = args.chunks[tile / args.m_tiles];
         const uint32_t idesc = idesc_e4m3_f32(128, ch.ncols);
-        const int k0 = KS * sp / SPLIT, k1 = KS * (sp + 1) / SPLIT;
         for (int ks = k0; ks < k1; ++ks, ++it) {
           const int b = it % NB, use = it / NB;
           if (!mbar_wait(&tempty[b], (use & 1) ^ 1, abort_flag)) {
@@ -349,12 +404,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     float acc_u[kG1 ? HB : 1];
     int it = 0;
     bool ok = true;
-    for (int unit = blockIdx.x; unit < num_units; unit += gridDim.x) {
-      const int tile = unit / SPLIT, sp = unit % SPLIT;
+    Schedule sched(num_tiles, KS, (int)gridDim.x, cta);
+    int tile, k0, k1;
+    while (sched.next(tile, k0, k1)) {
       const Chunk ch = args.chunks[tile / args.m_tiles];
       const int m = tile % args.m_tiles;
       const int ncols = ch.ncols;
-      const int k0 = KS * sp / SPLIT, k1 = KS * (sp + 1) / SPLIT;
       // weight block scales of this tile (one row for W2, gate and up rows for W13)
       named_bar(kBarAll, kEpiThreads);
       {
@@ -406,93 +461,91 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
 
-      // ---- split-K: publish this unit's partial; the last unit of the tile finishes ----
-      if (SPLIT > 1) {
-        // partial layout: [acc][row r][BN] floats; each thread owns HB contiguous floats
-        float* part = args.partials + (int64_t)unit * C::kPartialFloats;
+      // ---- stream-K: a partial segment publishes its fp32 partial; the contributor that
+      //      completes the tile's K range sums all contributions in K order and finishes ----
+      if (k0 != 0 || k1 != KS) {
+        // position of the tile in the stream-K step space
+        const StreamK& sk = sched.sk;
+        const int64_t tile_begin = (int64_t)(tile - sched.dp_tiles) * KS;
+        const int slot = sched.sk_begin() >= tile_begin ? 0 : 1;
+        float* part = args.partials + (int64_t)(2 * cta + slot) * C::kPartialFloats;
         store_row<HB>(part + (0 * 128 + r) * BN + half * HB, acc_g);
         if constexpr (kG1) store_row<HB>(part + (1 * 128 + r) * BN + half * HB, acc_u);
         __threadfence();
         named_bar(kBarAll, kEpiThreads);
+        const int cf = sk.cta_of(tile_begin), cl = sk.cta_of(tile_begin + KS - 1);
         if (tid_e == 0) {
-          const int done = atomicAdd(args.tile_counters + tile, 1);
-          const bool last = done == SPLIT - 1;
-          if (last) args.tile_counters[tile] = 0;  // ready for the next launch
+          const int done = atomicAdd(args.tile_counters + cf, k1 - k0) + (k1 - k0);
+          const bool last = done == KS;
+          if (last) args.tile_counters[cf] = 0;  // ready for the next launch
           *last_flag = last;
         }
         named_bar(kBarAll, kEpiThreads);
         if (!*last_flag) continue;
         __threadfence();
-        // deterministic: sum the partials in split order (all loads issued first)
-        const float* base = args.partials + (int64_t)(tile * SPLIT) * C::kPartialFloats;
-        constexpr int kRegs = kG1 ? 32 : 64;  // GEMM1 holds two accumulators
-        sum_partials<HB, kRegs>(acc_g, base + (0 * 128 + r) * BN + half * HB, SPLIT, sp,
-                                C::kPartialFloats);
+        constexpr int kRegs = 32;
+        sum_contributions<HB, kRegs>(acc_g, args.partials, (0 * 128 + r) * BN + half * HB,
+                                     C::kPartialFloats, sk, tile_begin, cf, cl);
         if constexpr (kG1)
-          sum_partials<HB, kRegs>(acc_u, base + (1 * 128 + r) * BN + half * HB, SPLIT, sp,
-                                  C::kPartialFloats);
+          sum_contributions<HB, kRegs>(acc_u, args.partials, (1 * 128 + r) * BN + half * HB,
+                                       C::kPartialFloats, sk, tile_begin, cf, cl);
       }
 
       if constexpr (kG1) {
         // ---- SwiGLU + FP8 hi/lo quantisation of C, per 128-column block m ----
-        // thread row r holds gate (x1) and up (x2) of C column 128 m + r
-        float* exh = ex + half * 128 * (CW + 1);  // [128 rows][CW + 1]
+        // thread row r holds gate (x1) and up (x2) of C column 128 m + r for this half's
+        // token columns; C goes to shared memory first so the accumulators die here
+        float* exh = ex + half * 128 * (HB + 1);  // [128 rows][HB + 1]
 #pragma unroll
-        for (int sc = 0; sc < HB / CW; ++sc) {
-          const int cbase = half * HB + sc * CW;
-          if (cbase < ncols) {
+        for (int i = 0; i < HB; ++i) exh[r * (HB + 1) + i] = acc_g[i] * silu(acc_u[i]);
+        named_bar(bar_half, 128);
+        // 4 threads per token column, 32 C columns each
+        const int i = tid_h >> 2, p = tid_h & 3;
+        const bool active = i < HB;
+        float vals[32];
+        float amax = 0.0f;
 #pragma unroll
-            for (int i = 0; i < CW; ++i)
-              exh[r * (CW + 1) + i] = acc_g[sc * CW + i] * silu(acc_u[sc * CW + i]);
-            named_bar(bar_half, 128);
-            // 4 threads per token column, 32 C columns each
-            const int i = tid_h >> 2, p = tid_h & 3;
-            float vals[32];
-            float amax = 0.0f;
-#pragma unroll
-            for (int k = 0; k < 32; ++k) {
-              vals[k] = exh[(p * 32 + k) * (CW + 1) + (i < CW ? i : 0)];
-              amax = fmaxf(amax, fabsf(vals[k]));
-            }
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
-            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
-            if (i < CW && cbase + i < ncols) {
-              const float inv = amax > 0.0f ? 448.0f / amax : 0.0f;
-              uint32_t hi[8], lo[8];
-#pragma unroll
-              for (int k = 0; k < 32; k += 4) {
-                float x[4], h[4], l[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) x[u] = vals[k + u] * inv;
-                const __nv_fp8x2_storage_t h01 =
-                    __nv_cvt_float2_to_fp8x2(make_float2(x[0], x[1]), __NV_SATFINITE, __NV_E4M3);
-                const __nv_fp8x2_storage_t h23 =
-                    __nv_cvt_float2_to_fp8x2(make_float2(x[2], x[3]), __NV_SATFINITE, __NV_E4M3);
-                const __half2_raw hr01 = __nv_cvt_fp8x2_to_halfraw2(h01, __NV_E4M3);
-                const __half2_raw hr23 = __nv_cvt_fp8x2_to_halfraw2(h23, __NV_E4M3);
-                const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&hr01));
-                const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&hr23));
-                h[0] = f01.x; h[1] = f01.y; h[2] = f23.x; h[3] = f23.y;
-#pragma unroll
-                for (int u = 0; u < 4; ++u) l[u] = x[u] - h[u];
-                const __nv_fp8x2_storage_t l01 =
-                    __nv_cvt_float2_to_fp8x2(make_float2(l[0], l[1]), __NV_SATFINITE, __NV_E4M3);
-                const __nv_fp8x2_storage_t l23 =
-                    __nv_cvt_float2_to_fp8x2(make_float2(l[2], l[3]), __NV_SATFINITE, __NV_E4M3);
-                hi[k / 4] = (uint32_t)h01 | ((uint32_t)h23 << 16);
-                lo[k / 4] = (uint32_t)l01 | ((uint32_t)l23 << 16);
-              }
-              const int64_t row = ch.row0 + cbase + i;
-              uint8_t* dst = args.cq + row * (2 * (int64_t)args.I) + m * 256 + p * 32;
-              reinterpret_cast<uint4*>(dst)[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-              reinterpret_cast<uint4*>(dst)[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-              reinterpret_cast<uint4*>(dst + 128)[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-              reinterpret_cast<uint4*>(dst + 128)[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
-              if (p == 0) args.c_scale[(int64_t)m * args.row_cap + row] = amax / 448.0f;
-            }
-            named_bar(bar_half, 128);
-          }
+        for (int k = 0; k < 32; ++k) {
+          vals[k] = exh[(p * 32 + k) * (HB + 1) + (active ? i : 0)];
+          amax = fmaxf(amax, fabsf(vals[k]));
         }
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+        if (active && half * HB + i < ncols) {
+          const float inv = amax > 0.0f ? 448.0f / amax : 0.0f;
+          uint32_t hi[8], lo[8];
+#pragma unroll
+          for (int k = 0; k < 32; k += 4) {
+            float x[4], h[4], l[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) x[u] = vals[k + u] * inv;
+            const __nv_fp8x2_storage_t h01 =
+                __nv_cvt_float2_to_fp8x2(make_float2(x[0], x[1]), __NV_SATFINITE, __NV_E4M3);
+            const __nv_fp8x2_storage_t h23 =
+                __nv_cvt_float2_to_fp8x2(make_float2(x[2], x[3]), __NV_SATFINITE, __NV_E4M3);
+            const __half2_raw hr01 = __nv_cvt_fp8x2_to_halfraw2(h01, __NV_E4M3);
+            const __half2_raw hr23 = __nv_cvt_fp8x2_to_halfraw2(h23, __NV_E4M3);
+            const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&hr01));
+            const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&hr23));
+            h[0] = f01.x; h[1] = f01.y; h[2] = f23.x; h[3] = f23.y;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) l[u] = x[u] - h[u];
+            const __nv_fp8x2_storage_t l01 =
+                __nv_cvt_float2_to_fp8x2(make_float2(l[0], l[1]), __NV_SATFINITE, __NV_E4M3);
+            const __nv_fp8x2_storage_t l23 =
+                __nv_cvt_float2_to_fp8x2(make_float2(l[2], l[3]), __NV_SATFINITE, __NV_E4M3);
+            hi[k / 4] = (uint32_t)h01 | ((uint32_t)h23 << 16);
+            lo[k / 4] = (uint32_t)l01 | ((uint32_t)l23 << 16);
+          }
+          const int64_t row = ch.row0 + half * HB + i;
+          uint8_t* dst = args.cq + row * (2 * (int64_t)args.I) + m * 256 + p * 32;
+          reinterpret_cast<uint4*>(dst)[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+          reinterpret_cast<uint4*>(dst)[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+          reinterpret_cast<uint4*>(dst + 128)[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          reinterpret_cast<uint4*>(dst + 128)[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+          if (p == 0) args.c_scale[(int64_t)m * args.row_cap + row] = amax / 448.0f;
+        }
+        named_bar(bar_half, 128);  // exh is reused by the next tile
       } else {
         // ---- weighted expert output rows, bf16, for the deterministic combine ----
         const int h = m * 128 + r;
@@ -540,9 +593,9 @@ cudaError_t launch_one(const CUtensorMap& a, const CUtensorMap& b, const GemmArg
 bool gemm_bn_supported(int bn) { return bn == 16 || bn == 32 || bn == 64; }
 
 size_t gemm_partial_bytes() {
-  // split-K is used only when tiles < 2 x SMs, so units < 4 x SMs; one partial tile is
-  // at most 2 accumulators x 128 rows x 64 columns of fp32 (GEMM1) or 128 x 64 (GEMM2)
-  return (size_t)4 * kMaxSms * 2 * 128 * 64 * sizeof(float);
+  // stream-K: two partial slots per CTA; one partial tile is at most 2 accumulators x 128
+  // rows x 64 columns of fp32 (GEMM1) or 128 x 64 (GEMM2)
+  return (size_t)2 * kMaxSms * 2 * 128 * 64 * sizeof(float);
 }
 
 cudaError_t launch_gemm1(int bn, const CUtensorMap& w13_map, const CUtensorMap& a_map,
