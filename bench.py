@@ -19,8 +19,12 @@ A sweep over configs 1, 2 and 4 (T = 1..8192, skewed routing) is attached as "sw
 own source into oracle/_ref by oracle/build_ref.sh) on the same workload. The reference
 has no CPU implementation of the path; its own code is CUDA, so it runs on the B200.
 
-Multi-GPU (torchrun, N>1): every rank runs the same per-rank workload on its own GPU;
-the time is the max over ranks and value counts the tokens of all ranks.
+Multi-GPU (torchrun, N>1): BASELINE config 3, the full 256-expert layer under expert
+parallelism (fmoe_b200.ep): rank r owns experts [r*256/N, (r+1)*256/N), holds 4096 tokens
+(weak scaling), routes them, dispatches FP8 rows + scales + (expert, weight) pairs with an
+NCCL all-to-all-v, runs the fused operator on what it received, and gets the partial
+outputs back with a second all-to-all-v. The step time is the max over ranks (CUDA events,
+all-reduce MAX); value counts the tokens of all ranks.
 """
 from __future__ import annotations
 
@@ -281,6 +285,90 @@ def sweep(seed, hbm_peak, fp8_peak):
     return res
 
 
+def run_ep(args, world, rank, local):
+    """Config 3: the 256-expert layer under expert parallelism over `world` ranks."""
+    from fmoe_b200 import ep
+
+    geo = W.DSV3
+    T = args.tokens if args.tokens_set else 4096
+    per = 256 // world
+    weights = W.make_expert_slice(geo, args.seed, rank * per, per, device="cuda")
+    acts = W.make_activations(geo, T, args.seed + 1009 * rank, device="cuda")
+    layer = ep.ExpertParallelMoE(weights=weights)
+    a4 = [acts[k] for k in W.OPERATOR_ARGS[:4]]
+    for _ in range(args.warmup):
+        layer.forward(*a4)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    gpu_index = local
+    pairs = []
+    with ClockSampler(gpu_index) as clk:
+        for _ in range(args.steps):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            layer.forward(*a4)
+            e1.record()
+            pairs.append((e0, e1))
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+    total = torch.tensor([sum(x.elapsed_time(y) for x, y in pairs)], device="cuda")
+    dist.all_reduce(total, op=dist.ReduceOp.MAX)
+    ms_per_step = float(total.item()) / args.steps
+    # stage breakdown (one extra timed pass, outside the measured steps)
+    layer.forward(*a4, timed=True)
+    tm = layer.timings
+    br = torch.tensor([tm.route_ms, tm.dispatch_ms, tm.compute_ms, tm.combine_ms], device="cuda")
+    dist.all_reduce(br, op=dist.ReduceOp.MAX)
+    # e2e: activations from pinned host memory, output back to the host, every step
+    names = W.OPERATOR_ARGS[:4]
+    host = {k: acts[k].cpu().pin_memory() for k in names}
+    dev = {k: torch.empty_like(acts[k]) for k in names}
+    out_host = torch.empty(T, geo.hidden, dtype=torch.bfloat16).pin_memory()
+    e2e_pairs = []
+    for i in range(args.steps):
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for k in names:
+            dev[k].copy_(host[k], non_blocking=True)
+        o = layer.forward(*[dev[k] for k in names])
+        out_host.copy_(o, non_blocking=True)
+        e1.record()
+        e2e_pairs.append((e0, e1))
+    torch.cuda.synchronize()
+    e2e_t = torch.tensor([sum(x.elapsed_time(y) for x, y in e2e_pairs)], device="cuda")
+    dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_t.item()) / args.steps
+    h2d = sum(host[k].numel() * host[k].element_size() for k in names)
+    rows = torch.tensor([0], device="cuda")
+    line = {
+        "metric": "MoE layer tokens/s (DS-V3 full 256-expert layer, expert parallel)",
+        "value": round(world * T / (ms_per_step * 1e-3), 1), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "e4m3 x e4m3 -> fp32 (tcgen05 kind::f8f6f4), fp32 block-scale promotion",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, FP8 128-block scales)",
+        "config": {"workload": "config3_dsv3_ep", "tokens_per_rank": T, "hidden": 7168,
+                   "intermediate": 2048, "experts": 256, "experts_per_rank": per, "top_k": 8,
+                   "n_group": 8, "topk_group": 4, "parallelism": f"ep{world}",
+                   "collectives": "NCCL all-to-all-v dispatch + combine, counts all-to-all",
+                   "l2": f"weights {per * 44.05 / 1000:.1f} GB per rank > L2"},
+        "breakdown_ms_max_over_ranks": {"route": round(float(br[0]), 3),
+                                        "dispatch": round(float(br[1]), 3),
+                                        "compute": round(float(br[2]), 3),
+                                        "combine": round(float(br[3]), 3)},
+        "clocks": clk.summary(),
+        "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": T * geo.hidden * 2},
+        "gpu_launches": (1 + 5) * args.steps,
+    }
+    return line
+
+
 def run_reference(args, rank):
     so = ROOT / "oracle" / "_ref" / "ref_kernel.so"
     base = {"metric": "MoE layer tokens/s (DS-V3 decode, T=64)", "impl": "reference"}
@@ -334,11 +422,14 @@ def main():
     ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--tokens", type=int, default=64)
+    ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     args = ap.parse_args()
+    args.tokens_set = args.tokens is not None
+    if args.tokens is None:
+        args.tokens = 64
     assert args.warmup >= 3, "at least 3 warm-up steps"
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -355,6 +446,14 @@ def main():
             print(json.dumps(line), flush=True)
         if world > 1:
             dist.destroy_process_group()
+        return
+
+    if world > 1:
+        line = run_ep(args, world, rank, local)
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        dist.barrier()
+        dist.destroy_process_group()
         return
 
     hbm_peak, bf16_peak, peak_src = load_peaks()

@@ -73,8 +73,8 @@ int validate(const fmoe_problem* p) {
   if (p->top_k < 1 || p->top_k > 32 ||
       p->top_k > p->topk_group * (p->num_experts / p->n_group))
     return fail(FMOE_ERR_VALUE, "top_k must be in [1, 32] and fit in the kept groups");
-  if (p->num_local_experts < 1 || p->num_local_experts > 64)
-    return fail(FMOE_ERR_VALUE, "num_local_experts must be in [1, 64]");
+  if (p->num_local_experts < 1 || p->num_local_experts > kMaxLocalExperts)
+    return fail(FMOE_ERR_VALUE, "num_local_experts must be in [1, 256]");
   if (p->hidden_size < 128 || p->hidden_size % 128 != 0 || p->hidden_size > 16384)
     return fail(FMOE_ERR_VALUE, "hidden_size must be a positive multiple of 128 (<= 16384)");
   if (p->intermediate_size < 128 || p->intermediate_size % 128 != 0 ||
@@ -169,6 +169,8 @@ int carve(const fmoe_problem* p, void* ws, size_t ws_bytes, Carved* c) {
 RouteArgs route_args(const fmoe_problem* p, const Carved& c, const float* logits,
                      const void* bias, int bn) {
   RouteArgs a;
+  a.in_idx = nullptr;
+  a.in_w = nullptr;
   a.logits = logits;
   a.bias = static_cast<const uint16_t*>(bias);
   a.T = p->num_tokens;
@@ -196,11 +198,14 @@ RouteArgs route_args(const fmoe_problem* p, const Carved& c, const float* logits
 }
 
 int launch_route(const fmoe_problem* p, const Carved& c, const float* logits, const void* bias,
-                 int bn, cudaStream_t stream) {
-  // meta words and the split-K counters are contiguous: one small memset per call
+                 int bn, cudaStream_t stream, const int* in_idx = nullptr,
+                 const float* in_w = nullptr) {
+  // meta words and the stream-K counters are contiguous: one small memset per call
   FMOE_CUDA_TRY(cudaMemsetAsync(c.at<int>(c.L.meta), 0, c.L.counters - c.L.meta +
                                 kTileCounters * sizeof(int), stream));
-  const RouteArgs ra = route_args(p, c, logits, bias, bn);
+  RouteArgs ra = route_args(p, c, logits, bias, bn);
+  ra.in_idx = in_idx;
+  ra.in_w = in_w;
   FMOE_CUDA_TRY(launch_pdl(route_plan_kernel, dim3((unsigned)c.L.n_route_ctas),
                            dim3(kRouteTokensPerCta * 32), 0, stream, ra));
   return FMOE_OK;
@@ -229,16 +234,22 @@ extern "C" int fmoe_workspace_size(const fmoe_problem* p, size_t* bytes) {
   return FMOE_OK;
 }
 
-extern "C" int fmoe_forward(const fmoe_problem* p, const fmoe_tensors* t, void* workspace,
-                            size_t workspace_bytes, void* stream_ptr) {
+namespace fmoe {
+namespace {
+int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_idx,
+                const float* in_w, void* workspace, size_t workspace_bytes, void* stream_ptr) {
   int v = validate(p);
   if (v != FMOE_OK) return v;
   if (!t) return fail(FMOE_ERR_VALUE, "tensors must not be NULL");
   if (p->num_tokens == 0) return FMOE_OK;  // empty batch: nothing to write
-  const void* ptrs[] = {t->routing_logits, t->routing_bias, t->hidden_states,
+  if (in_idx && (!in_w || !aligned(in_idx, 16) || !aligned(in_w, 16)))
+    return fail(FMOE_ERR_VALUE, "topk_idx / topk_w must be non-NULL and 16-byte aligned");
+  const void* ptrs[] = {in_idx ? (const void*)in_idx : t->routing_logits,
+                        in_idx ? (const void*)in_w : t->routing_bias, t->hidden_states,
                         t->hidden_states_scale, t->gemm1_weights, t->gemm1_weights_scale,
                         t->gemm2_weights, t->gemm2_weights_scale, t->output};
-  const char* names[] = {"routing_logits", "routing_bias", "hidden_states",
+  const char* names[] = {in_idx ? "topk_idx" : "routing_logits",
+                         in_idx ? "topk_w" : "routing_bias", "hidden_states",
                          "hidden_states_scale", "gemm1_weights", "gemm1_weights_scale",
                          "gemm2_weights", "gemm2_weights_scale", "output"};
   for (int i = 0; i < 9; ++i) {
@@ -255,7 +266,7 @@ extern "C" int fmoe_forward(const fmoe_problem* p, const fmoe_tensors* t, void* 
   const int H = p->hidden_size, I = p->intermediate_size, EL = p->num_local_experts;
 
   if ((v = mark_stage(0, stream)) != FMOE_OK) return v;
-  v = launch_route(p, c, t->routing_logits, t->routing_bias, bn, stream);
+  v = launch_route(p, c, t->routing_logits, t->routing_bias, bn, stream, in_idx, in_w);
   if (v != FMOE_OK) return v;
   if ((v = mark_stage(1, stream)) != FMOE_OK) return v;
 
@@ -346,6 +357,20 @@ extern "C" int fmoe_forward(const fmoe_problem* p, const fmoe_tensors* t, void* 
   FMOE_CUDA_TRY(launch_pdl(combine_kernel, dim3((unsigned)T, (unsigned)((H / 8 + 127) / 128)),
                            dim3(128), 0, stream, ca));
   return mark_stage(5, stream);
+}
+}  // namespace
+}  // namespace fmoe
+
+extern "C" int fmoe_forward(const fmoe_problem* p, const fmoe_tensors* t, void* workspace,
+                            size_t workspace_bytes, void* stream_ptr) {
+  return run_forward(p, t, nullptr, nullptr, workspace, workspace_bytes, stream_ptr);
+}
+
+extern "C" int fmoe_forward_routed(const fmoe_problem* p, const int32_t* topk_idx,
+                                   const float* topk_w, const fmoe_tensors* t, void* workspace,
+                                   size_t workspace_bytes, void* stream_ptr) {
+  if (!topk_idx || !topk_w) return fail(FMOE_ERR_VALUE, "topk_idx / topk_w must not be NULL");
+  return run_forward(p, t, topk_idx, topk_w, workspace, workspace_bytes, stream_ptr);
 }
 
 extern "C" int fmoe_set_stage_events(void* const* events) {

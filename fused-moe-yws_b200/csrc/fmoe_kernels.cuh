@@ -15,6 +15,8 @@ namespace fmoe {
 struct RouteArgs {
   const float* logits;     // [T, E]
   const uint16_t* bias;    // [E] bf16 bits
+  const int* in_idx;       // routed mode: given [T, K] expert ids (logits unused); else null
+  const float* in_w;       // routed mode: given [T, K] weights
   int64_t T;
   int E, n_group, topk_group, top_k, E_local, local_offset;
   float rsf;

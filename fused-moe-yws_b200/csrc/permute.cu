@@ -35,7 +35,7 @@ __global__ void __launch_bounds__(256) scatter_gather_kernel(ScatterArgs a) {
   __shared__ int s_le[kMaxEntries];
   __shared__ int s_row[kMaxEntries];
   __shared__ int s_list[kMaxEntries];
-  __shared__ int s_base[64];
+  __shared__ int s_base[kMaxLocalExperts];
   __shared__ int s_nlocal;
 
   const int tid = threadIdx.x;

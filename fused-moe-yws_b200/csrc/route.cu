@@ -57,11 +57,11 @@ __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
   __shared__ float s_sc[kWarps][kMaxE];
   __shared__ float s_wb[kWarps][kMaxE];
   __shared__ float s_gscore[kWarps][kMaxGroups];
-  __shared__ int s_cnt[64];
+  __shared__ int s_cnt[kMaxLocalExperts];
   __shared__ int s_is_last;
-  __shared__ int s_tot[64];
-  __shared__ int s_off[65];
-  __shared__ int s_choff[65];
+  __shared__ int s_tot[kMaxLocalExperts];
+  __shared__ int s_off[kMaxLocalExperts + 1];
+  __shared__ int s_choff[kMaxLocalExperts + 1];
   __shared__ int s_sel[kWarps][32];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -73,7 +73,16 @@ __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
   __syncthreads();
 
   const int64_t t = (int64_t)blockIdx.x * kWarps + warp;
-  if (t < a.T) {
+  if (t < a.T && a.in_idx) {
+    // routed mode: (expert, weight) pairs computed elsewhere (expert-parallel dispatch)
+    if (lane < K) {
+      const int e = a.in_idx[t * K + lane];
+      a.topk_idx[t * K + lane] = e;
+      a.topk_w[t * K + lane] = a.in_w[t * K + lane];
+      const int le = e - a.local_offset;
+      if (e >= 0 && le >= 0 && le < a.E_local) atomicAdd(&s_cnt[le], 1);
+    }
+  } else if (t < a.T) {
     // 1) sigmoid + bias (strided, coalesced loads)
     const float* lrow = a.logits + t * E;
     for (int e = lane; e < E; e += 32) {
@@ -192,7 +201,7 @@ __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
   }
   __syncthreads();
   if (warp == 0) {
-    // exclusive scans over experts (two experts per lane covers E_local <= 64)
+    // exclusive scans over experts, 32 at a time
     int run_off = 0, run_ch = 0;
     for (int base = 0; base < a.E_local; base += 32) {
       const int e = base + lane;

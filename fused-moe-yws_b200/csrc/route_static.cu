@@ -110,6 +110,8 @@ extern "C" int fmoe_route_static(const fmoe_problem* p, const float* routing_log
 
   const int bn = p->tile_n ? p->tile_n : autotune_tile_n(p->num_tokens);
   RouteArgs a;
+  a.in_idx = nullptr;
+  a.in_w = nullptr;
   a.logits = routing_logits;
   a.bias = static_cast<const uint16_t*>(routing_bias);
   a.T = p->num_tokens;

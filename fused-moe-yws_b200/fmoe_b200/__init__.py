@@ -31,7 +31,8 @@ FMOE_OK, FMOE_ERR_VALUE, FMOE_ERR_TYPE, FMOE_ERR_RUNTIME, FMOE_ERR_WORKSPACE, FM
 
 EXPORTED_SYMBOLS = ("fmoe_abi_version", "fmoe_last_error", "fmoe_validate", "fmoe_workspace_size",
                     "fmoe_autotune_tile_n", "fmoe_forward", "fmoe_route", "fmoe_read_device_error",
-                    "fmoe_plan_view_get", "fmoe_set_stage_events", "fmoe_route_static")
+                    "fmoe_plan_view_get", "fmoe_set_stage_events", "fmoe_route_static",
+                    "fmoe_forward_routed")
 
 
 class FmoeProblem(ctypes.Structure):
@@ -90,6 +91,9 @@ def load_library(path: Path | str | None = None):
         lib.fmoe_plan_view_get.argtypes = [ctypes.POINTER(FmoeProblem), ctypes.c_void_p,
                                            ctypes.POINTER(FmoePlanView)]
         lib.fmoe_set_stage_events.argtypes = [ctypes.c_void_p]
+        lib.fmoe_forward_routed.argtypes = [ctypes.POINTER(FmoeProblem), ctypes.c_void_p,
+                                            ctypes.c_void_p, ctypes.POINTER(FmoeTensors),
+                                            ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
         for name in EXPORTED_SYMBOLS:
             if not hasattr(lib, name):
                 raise RuntimeError(f"{p} does not export {name}")
@@ -240,6 +244,48 @@ def kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale, gem
                               workspace.numel(), stream)
     if rc != FMOE_OK:
         _raise(lib, rc, "kernel")
+    return out
+
+
+def forward_routed(topk_idx, topk_w, hidden_states, hidden_states_scale, gemm1_weights,
+                   gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+                   local_expert_offset: int, num_experts: int = 256, *, out=None,
+                   tile_n: int = 0, n_group=None, topk_group=None) -> torch.Tensor:
+    """The operator on precomputed routing (``topk_idx`` int32 / ``topk_w`` fp32 [T, K]).
+
+    Returns per-token sums over the local experts [offset, offset + E_local) in bf16.
+    """
+    T, K = topk_idx.shape
+    EL, two_i, H = gemm1_weights.shape
+    I = two_i // 2
+    _check_tensor(topk_idx, "topk_idx", (T, K), torch.int32)
+    _check_tensor(topk_w, "topk_w", (T, K), _F32)
+    _check_tensor(hidden_states, "hidden_states", (T, H), _F8)
+    _check_tensor(hidden_states_scale, "hidden_states_scale", (H // 128, T), _F32)
+    _check_tensor(gemm1_weights, "gemm1_weights", (EL, 2 * I, H), _F8)
+    _check_tensor(gemm1_weights_scale, "gemm1_weights_scale", (EL, 2 * I // 128, H // 128), _F32)
+    _check_tensor(gemm2_weights, "gemm2_weights", (EL, H, I), _F8)
+    _check_tensor(gemm2_weights_scale, "gemm2_weights_scale", (EL, H // 128, I // 128), _F32)
+    lib = load_library()
+    ng, kg, _ = ROUTING_BY_EXPERTS.get(num_experts, (n_group, topk_group, K))
+    prob = make_problem(T, num_experts, EL, H, I, local_expert_offset, 1.0,
+                        n_group or ng, topk_group or kg, K, tile_n)
+    dev = hidden_states.device
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    if T == 0:
+        return out
+    nbytes = workspace_bytes(prob)
+    ws = Workspace.get(dev, nbytes)
+    tens = FmoeTensors(0, 0, hidden_states.data_ptr(), hidden_states_scale.data_ptr(),
+                       gemm1_weights.data_ptr(), gemm1_weights_scale.data_ptr(),
+                       gemm2_weights.data_ptr(), gemm2_weights_scale.data_ptr(), out.data_ptr())
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = lib.fmoe_forward_routed(ctypes.byref(prob), topk_idx.data_ptr(), topk_w.data_ptr(),
+                                     ctypes.byref(tens), ws.data_ptr(), ws.numel(), stream)
+    if rc != FMOE_OK:
+        _raise(lib, rc, "forward_routed")
     return out
 
 

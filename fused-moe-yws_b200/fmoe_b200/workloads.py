@@ -122,6 +122,25 @@ def make_weights(geo: Geometry, seed: int, device="cpu", experts=None):
                 gemm2_weights_scale=s2)
 
 
+def make_expert_slice(geo: Geometry, seed: int, first: int, count: int, device="cpu"):
+    """Weights of global experts [first, first + count) (expert-parallel rank slice); the
+    values are those `make_weights` gives the same experts, since each expert has its own
+    generator keyed by (seed, expert id)."""
+    H, I = geo.hidden, geo.inter
+    w13 = torch.empty(count, 2 * I, H, dtype=torch.float8_e4m3fn, device=device)
+    s13 = torch.empty(count, 2 * I // 128, H // 128, dtype=torch.float32, device=device)
+    w2 = torch.empty(count, H, I, dtype=torch.float8_e4m3fn, device=device)
+    s2 = torch.empty(count, H // 128, I // 128, dtype=torch.float32, device=device)
+    for j in range(count):
+        q13, a13, q2, a2 = make_expert(geo, seed, first + j, device)
+        w13[j].copy_(q13)
+        s13[j].copy_(a13)
+        w2[j].copy_(q2)
+        s2[j].copy_(a2)
+    return dict(gemm1_weights=w13, gemm1_weights_scale=s13, gemm2_weights=w2,
+                gemm2_weights_scale=s2)
+
+
 def make_inputs(geo: Geometry, T: int, seed: int, device="cpu", skew_hot: int = 0,
                 local_expert_offset: int = 0, experts=None):
     acts = make_activations(geo, T, seed, device, skew_hot, local_expert_offset)

@@ -43,7 +43,7 @@ enum fmoe_status {
 typedef struct fmoe_problem {
   int64_t num_tokens;          /* T: routing_logits.shape[0] */
   int32_t num_experts;         /* E_global: routing_logits.shape[1] (<= 256, multiple of n_group) */
-  int32_t num_local_experts;   /* E_local: gemm1_weights.shape[0] (<= 64) */
+  int32_t num_local_experts;   /* E_local: gemm1_weights.shape[0] (<= 256) */
   int32_t hidden_size;         /* H: multiple of 128, <= 16384 */
   int32_t intermediate_size;   /* I: multiple of 128, <= 16384 */
   int32_t top_k;               /* experts per token (<= 32) */
@@ -99,6 +99,16 @@ int fmoe_autotune_tile_n(int64_t num_tokens);
  * (a cudaStream_t; NULL = legacy default stream). One call at a time per workspace. */
 int fmoe_forward(const fmoe_problem* p, const fmoe_tensors* t, void* workspace,
                  size_t workspace_bytes, void* stream);
+
+/* The operator on routing decided elsewhere: topk_idx/topk_w ([T, top_k] global expert ids
+ * and weights, device pointers, 16-byte aligned) replace routing_logits/routing_bias, which
+ * are ignored. Used by the expert-parallel layer, where the rank that owns a token routes it
+ * once and ships (ids, weights) with the token to the ranks that own those experts. It
+ * replaces the reference's local-slice hook (local_expert_offset, kernel.cu:540-544,
+ * :572-586, :857-859) for tokens arriving from other ranks. */
+int fmoe_forward_routed(const fmoe_problem* p, const int32_t* topk_idx, const float* topk_w,
+                        const fmoe_tensors* t, void* workspace, size_t workspace_bytes,
+                        void* stream);
 
 /* Routing only (replaces sigmoid_bias_kernel + routing_select_kernel,
  * kernel.cu:388-516), for parity tests and the expert-parallel dispatch.

@@ -5,5 +5,6 @@ Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench
 ``fused-moe-yws_b200/`` never does. See ``fmoe_ref.py`` (PyTorch/C restatement of the
 reference algorithm, parity pinned by ``tests/golden``) and ``fmoe_oracle.c``.
 """
-from .fmoe_ref import (build, dequant_act, dequant_weight, moe_forward, plan, route,  # noqa: F401
-                       route_definition, route_margin, sigmoid)
+from .fmoe_ref import (build, dequant_act, dequant_weight, moe_forward,  # noqa: F401
+                       moe_forward_routed, plan, route, route_definition, route_margin,
+                       sigmoid)

@@ -185,11 +185,29 @@ def moe_forward(routing_logits, routing_bias, hidden_states, hidden_states_scale
     dequantised, one at a time, so the DS-V3 shapes fit in host memory. A dict passed
     as ``weight_cache`` keeps the dequantised experts between calls on the same weights.
     """
-    T = routing_logits.shape[0]
-    E_local, two_i, H = gemm1_weights.shape
-    I = two_i // 2
     idx, w = route(routing_logits, routing_bias, n_group, topk_group, top_k,
                    routed_scaling_factor)
+    out = moe_forward_routed(idx, w, hidden_states, hidden_states_scale, gemm1_weights,
+                             gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+                             local_expert_offset, weight_cache=weight_cache, fp32=True)
+    res = out.to(torch.bfloat16)
+    if return_aux:
+        return res, dict(topk_idx=idx, topk_w=w, out_f32=out)
+    return res
+
+
+def moe_forward_routed(topk_idx, topk_w, hidden_states, hidden_states_scale, gemm1_weights,
+                       gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+                       local_expert_offset: int, weight_cache: dict | None = None,
+                       fp32: bool = False):
+    """The operator after routing: out[t] = sum over (t, k) with a local expert of
+    w[t, k] * GEMM2(SwiGLU(GEMM1(A_t))) (kernel.cu:761-891), fp32 on the host cores.
+    Returns fp32 [T, H] when ``fp32`` else bf16."""
+    idx = _np(topk_idx).astype(np.int32)
+    w = _np(topk_w).astype(np.float32)
+    T = idx.shape[0]
+    E_local, two_i, H = gemm1_weights.shape
+    I = two_i // 2
     out = torch.zeros(T, H, dtype=torch.float32)
     w_t = torch.from_numpy(w)
     for le in range(E_local):
@@ -213,10 +231,7 @@ def moe_forward(routing_logits, routing_bias, hidden_states, hidden_states_scale
         o = c @ w2.t()
         wt = w_t[torch.from_numpy(tok), torch.from_numpy(kk)].unsqueeze(1)
         out.index_add_(0, torch.from_numpy(tok), o * wt)
-    res = out.to(torch.bfloat16)
-    if return_aux:
-        return res, dict(topk_idx=idx, topk_w=w, out_f32=out)
-    return res
+    return out if fp32 else out.to(torch.bfloat16)
 
 
 def route_margin(logits, bias, n_group, topk_group, top_k) -> float:

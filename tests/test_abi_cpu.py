@@ -39,7 +39,7 @@ def _prob(fmoe, **kw):
 
 @pytest.mark.parametrize("field,value", [
     ("num_tokens", -1), ("num_experts", 0), ("num_experts", 512), ("n_group", 7),
-    ("topk_group", 9), ("top_k", 0), ("top_k", 33), ("num_local_experts", 65),
+    ("topk_group", 9), ("top_k", 0), ("top_k", 33), ("num_local_experts", 257),
     ("hidden_size", 100), ("intermediate_size", 64), ("tile_n", 48)])
 def test_validate_rejects(fmoe, field, value):
     lib = fmoe.load_library()

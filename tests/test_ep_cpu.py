@@ -1,0 +1,157 @@
+"""Expert-parallel layer: host-side exchange logic on CPU ranks (gloo).
+
+The routing and the per-rank expert compute are the CPU oracle, so these tests check the
+dispatch / combine logic of fmoe_b200.ep (destination masks, ordering, all-to-all-v,
+unpacking, rank-ordered reduction) against the oracle's single-process full layer, on 2
+and 4 ranks. A failure test kills one rank before the exchange and checks that the other
+rank gets an error from its collective within the process-group timeout instead of
+waiting forever.
+"""
+import datetime
+import os
+import socket
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parent.parent
+for _p in (ROOT, ROOT / "fused-moe-yws_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+GEO_E, GEO_H, GEO_I, NG, KG, K = 16, 256, 128, 4, 2, 4
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _init(rank, world, port, timeout_s=60):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def _geo():
+    from fmoe_b200 import workloads as W
+
+    return W.Geometry(hidden=GEO_H, inter=GEO_I, num_experts=GEO_E, num_local=GEO_E,
+                      n_group=NG, topk_group=KG, top_k=K)
+
+
+def _ep_worker(rank, world, port, T, result_q):
+    import oracle
+    from fmoe_b200 import ep
+    from fmoe_b200 import workloads as W
+
+    _init(rank, world, port)
+    torch.set_num_threads(1)
+    geo = _geo()
+    full = W.make_weights(geo, seed=9, device="cpu")
+    per = GEO_E // world
+    sl = slice(rank * per, (rank + 1) * per)
+    local = {k: v[sl].contiguous() for k, v in full.items()}
+    acts = W.make_activations(geo, T + rank, seed=100 + rank, device="cpu")
+
+    def route_fn(logits, bias):
+        idx, w = oracle.route(logits, bias, NG, KG, K, 2.5)
+        return torch.from_numpy(idx), torch.from_numpy(w)
+
+    def local_fn(idx, w, hs, sc, offset):
+        return oracle.moe_forward_routed(idx, w, hs, sc, local["gemm1_weights"],
+                                         local["gemm1_weights_scale"], local["gemm2_weights"],
+                                         local["gemm2_weights_scale"], offset)
+
+    layer = ep.ExpertParallelMoE(num_experts=GEO_E, n_group=NG, topk_group=KG, top_k=K,
+                                 routed_scaling_factor=2.5, route_fn=route_fn,
+                                 local_fn=local_fn)
+    out = layer.forward(acts["routing_logits"], acts["routing_bias"], acts["hidden_states"],
+                        acts["hidden_states_scale"])
+    ref = oracle.moe_forward(*W.operator_args({**acts, **full}), 0, 2.5, NG, KG, K)
+    err = (out.float() - ref.float()).abs()
+    rel = float((out.float() - ref.float()).norm() / ref.float().norm().clamp_min(1e-12))
+    ok = bool((err <= 2e-2 + 2e-2 * ref.float().abs()).all())
+    result_q.put((rank, ok, rel, tuple(out.shape)))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_ep_matches_full_layer(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, 24, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=240) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, ok, rel, shape in sorted(results):
+        assert shape == (24 + rank, GEO_H)
+        assert ok and rel < 1e-2, (rank, rel)
+
+
+def test_pack_unpack_roundtrip():
+    from fmoe_b200 import ep
+    from fmoe_b200 import workloads as W
+
+    acts = W.make_activations(_geo(), 10, seed=3)
+    idx = torch.randint(0, GEO_E, (10, K), dtype=torch.int32)
+    w = torch.rand(10, K)
+    tokens = torch.tensor([7, 1, 3])
+    buf = ep.pack_rows(acts["hidden_states"], acts["hidden_states_scale"], idx, w, tokens)
+    hs, sc, ii, ww = ep.unpack_rows(buf, GEO_H, K)
+    assert torch.equal(hs.view(torch.uint8), acts["hidden_states"].view(torch.uint8)[tokens])
+    assert torch.equal(sc, acts["hidden_states_scale"][:, tokens])
+    assert torch.equal(ii, idx[tokens]) and torch.equal(ww, w[tokens])
+
+
+def _dying_worker(rank, world, port, result_q):
+    from fmoe_b200 import workloads as W
+    from fmoe_b200 import ep
+
+    _init(rank, world, port, timeout_s=5)
+    if rank == 1:
+        os._exit(3)  # the rank dies between steps, before the exchange
+    geo = _geo()
+    acts = W.make_activations(geo, 8, seed=1)
+
+    def route_fn(logits, bias):
+        idx = torch.zeros(logits.shape[0], K, dtype=torch.int32)
+        idx[:, 1] = GEO_E - 1  # one route on the peer's experts
+        return idx, torch.ones(logits.shape[0], K)
+
+    layer = ep.ExpertParallelMoE(num_experts=GEO_E, n_group=NG, topk_group=KG, top_k=K,
+                                 route_fn=route_fn, local_fn=lambda *a: None)
+    try:
+        layer.forward(acts["routing_logits"], acts["routing_bias"], acts["hidden_states"],
+                      acts["hidden_states_scale"])
+        result_q.put((rank, "no error"))
+    except Exception as e:  # the collective must fail, not hang
+        result_q.put((rank, type(e).__name__))
+
+
+def test_ep_peer_failure_is_reported():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_dying_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    rank, what = q.get(timeout=120)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert rank == 0 and what != "no error"

@@ -1,0 +1,90 @@
+"""Expert parallelism on B200s over NCCL (needs >= 2 GPUs; skipped otherwise).
+
+Each rank owns 256 / N consecutive experts. The EP layer's output for a rank's tokens is
+compared with the single-GPU operator run on the same tokens with all 256 experts local
+(E_local = 256), and the 256-expert single-GPU call is itself checked against the sum of
+its eight 32-expert slices (each slice is checked against the CPU oracle elsewhere).
+"""
+import datetime
+import os
+import socket
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parent.parent
+for _p in (ROOT, ROOT / "fused-moe-yws_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _close(out, ref):
+    out, ref = out.float().cpu(), ref.float().cpu()
+    ok = bool((((out - ref).abs()) <= 2e-2 + 2e-2 * ref.abs()).all())
+    rel = float((out - ref).norm() / ref.norm().clamp_min(1e-12))
+    return ok, rel
+
+
+def _worker(rank, world, port, T, q):
+    import fmoe_b200
+    from dataclasses import replace
+    from fmoe_b200 import ep
+    from fmoe_b200 import workloads as W
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank),
+                            timeout=datetime.timedelta(seconds=120))
+    geo = W.DSV3
+    per = 256 // world
+    full = W.make_expert_slice(geo, 7, 0, 256, device="cuda")
+    local = {k: v[rank * per:(rank + 1) * per].contiguous() for k, v in full.items()}
+    acts = W.make_activations(geo, T, 500 + rank, device="cuda")
+    layer = ep.ExpertParallelMoE(weights=local)
+    out = layer.forward(acts["routing_logits"], acts["routing_bias"], acts["hidden_states"],
+                        acts["hidden_states_scale"])
+    args = [acts[k] for k in W.OPERATOR_ARGS[:4]] + [full[k] for k in W.OPERATOR_ARGS[4:]]
+    ref = fmoe_b200.kernel(*args, 0, 2.5)
+    slices = torch.zeros(T, geo.hidden, dtype=torch.float32, device="cuda")
+    for s in range(8):
+        sl = {k: v[32 * s:32 * (s + 1)].contiguous() for k, v in full.items()}
+        a = [acts[k] for k in W.OPERATOR_ARGS[:4]] + [sl[k] for k in W.OPERATOR_ARGS[4:]]
+        slices += fmoe_b200.kernel(*a, 32 * s, 2.5).float()
+    torch.cuda.synchronize()
+    q.put((rank, _close(out, ref), _close(ref, slices)))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_two_gpus_matches_full_layer():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, 256, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, (ok_ep, rel_ep), (ok_sl, rel_sl) in res:
+        assert ok_ep and rel_ep < 1e-2, (rank, rel_ep)
+        assert ok_sl and rel_sl < 1e-2, (rank, rel_sl)
