@@ -146,12 +146,12 @@ def layer_bytes(T, active):
     return active * BYTES_PER_EXPERT + T * (7168 + 224 + 1024) + T * 7168 * 2
 
 
-def time_device(inp, steps, warmup, flush, stage=False):
+def time_device(inp, steps, warmup, flush, stage=False, tile_n=0):
     """Per-call device time (ms) with inputs resident; L2 flushed between calls."""
     args = W.operator_args(inp)
     out = torch.empty(args[0].shape[0], 7168, dtype=torch.bfloat16, device="cuda")
     for _ in range(warmup):
-        fmoe_b200.kernel(*args, 0, 2.5, out=out)
+        fmoe_b200.kernel(*args, 0, 2.5, out=out, tile_n=tile_n)
     torch.cuda.synchronize()
     pairs, timers = [], []
     for _ in range(steps):
@@ -162,12 +162,12 @@ def time_device(inp, steps, warmup, flush, stage=False):
             st = fmoe_b200.StageTimer()
             with st:
                 e0.record()
-                fmoe_b200.kernel(*args, 0, 2.5, out=out)
+                fmoe_b200.kernel(*args, 0, 2.5, out=out, tile_n=tile_n)
                 e1.record()
             timers.append(st)
         else:
             e0.record()
-            fmoe_b200.kernel(*args, 0, 2.5, out=out)
+            fmoe_b200.kernel(*args, 0, 2.5, out=out, tile_n=tile_n)
             e1.record()
         pairs.append((e0, e1))
     torch.cuda.synchronize()
@@ -176,7 +176,7 @@ def time_device(inp, steps, warmup, flush, stage=False):
     return ms, stages, out
 
 
-def time_graph(inp, steps, warmup, flush):
+def time_graph(inp, steps, warmup, flush, tile_n=0):
     """Per-call device time (ms) of the operator replayed from a CUDA graph (all five
     kernels and the workspace memset captured once); L2 flushed between replays."""
     args = W.operator_args(inp)
@@ -185,11 +185,11 @@ def time_graph(inp, steps, warmup, flush):
     side.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(side):
         for _ in range(warmup):
-            fmoe_b200.kernel(*args, 0, 2.5, out=out)
+            fmoe_b200.kernel(*args, 0, 2.5, out=out, tile_n=tile_n)
     torch.cuda.current_stream().wait_stream(side)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph):
-        fmoe_b200.kernel(*args, 0, 2.5, out=out)
+        fmoe_b200.kernel(*args, 0, 2.5, out=out, tile_n=tile_n)
     for _ in range(warmup):
         graph.replay()
     torch.cuda.synchronize()
@@ -257,29 +257,39 @@ def cpu_baseline(T, seed):
             "sample": f"one call of the T={T} DS-V3 layer (dequantise + fp32 GEMMs), {dt:.2f} s"}
 
 
-def sweep(seed, hbm_peak, fp8_peak):
+def sweep(seed, hbm_peak, fp8_peak, tiles=(0,)):
+    """Configs 1, 2 and 4 over T; `tiles` lists the token tiles timed per case (0 = the
+    autotune table). Tiles above 16 are skipped for T < 64 and 128 for T < 512."""
     res = []
+    lib = fmoe_b200.load_library()
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     for cfg, T, skew in [("config1", 1, 0), ("config1", 4, 0), ("config1", 16, 0),
                          ("config1", 64, 0), ("config2", 512, 0), ("config2", 2048, 0),
                          ("config2", 4096, 0), ("config2", 8192, 0), ("config4", 4096, 8)]:
         inp = make_workload(T, seed, skew)
         rows, active = routed_stats(inp)
-        ms_e, stages, _ = time_device(inp, steps=10, warmup=3, flush=flush, stage=True)
-        ms, _ = time_graph(inp, steps=10, warmup=3, flush=flush)
-        t = statistics.median(ms)
-        st = [statistics.median(s[i] for s in stages) for i in range(5)]
         b = layer_bytes(T, active)
-        res.append({"config": cfg, "T": T, "skew_hot": skew, "rows": rows,
-                    "active_experts": active, "us_per_call": round(t * 1e3, 1),
-                    "us_per_call_eager": round(statistics.median(ms_e) * 1e3, 1),
-                    "tokens_per_s": round(T / (t * 1e-3), 1),
-                    "hbm_gbs": round(b / (t * 1e-3) / 1e9, 1),
-                    "hbm_frac": round(b / (t * 1e-3) / 1e9 / hbm_peak, 3),
-                    "fp8_tflops": round(rows * FLOP_PER_ROW / (t * 1e-3) / 1e12, 1),
-                    "fp8_frac": round(rows * FLOP_PER_ROW / (t * 1e-3) / 1e12 / fp8_peak, 3),
-                    "stage_us": dict(zip(fmoe_b200.StageTimer.STAGES,
-                                         [round(x * 1e3, 1) for x in st]))})
+        for tile in tiles:
+            if (tile > 16 and T < 64) or (tile == 128 and T < 512):
+                continue
+            ms_e, stages, _ = time_device(inp, steps=10, warmup=3, flush=flush, stage=True,
+                                          tile_n=tile)
+            ms, _ = time_graph(inp, steps=10, warmup=3, flush=flush, tile_n=tile)
+            t = statistics.median(ms)
+            st = [statistics.median(s[i] for s in stages) for i in range(5)]
+            res.append({"config": cfg, "T": T, "skew_hot": skew, "rows": rows,
+                        "active_experts": active,
+                        "tile_n": tile or lib.fmoe_autotune_tile_n(T),
+                        "us_per_call": round(t * 1e3, 1),
+                        "us_per_call_eager": round(statistics.median(ms_e) * 1e3, 1),
+                        "tokens_per_s": round(T / (t * 1e-3), 1),
+                        "hbm_gbs": round(b / (t * 1e-3) / 1e9, 1),
+                        "hbm_frac": round(b / (t * 1e-3) / 1e9 / hbm_peak, 3),
+                        "fp8_tflops": round(rows * FLOP_PER_ROW / (t * 1e-3) / 1e12, 1),
+                        "fp8_frac": round(rows * FLOP_PER_ROW / (t * 1e-3) / 1e12 / fp8_peak,
+                                          3),
+                        "stage_us": dict(zip(fmoe_b200.StageTimer.STAGES,
+                                             [round(x * 1e3, 1) for x in st]))})
         del inp
         torch.cuda.empty_cache()
     return res
@@ -426,6 +436,8 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--sweep-tiles", default="0",
+                    help="comma-separated token tiles timed per sweep case (0 = autotune)")
     args = ap.parse_args()
     args.tokens_set = args.tokens is not None
     if args.tokens is None:
@@ -534,7 +546,8 @@ def main():
         if not args.no_cpu and world == 1:
             line["cpu_baseline"] = cpu_baseline(T, args.seed)
         if not args.no_sweep and world == 1:
-            line["sweep"] = sweep(args.seed, hbm_peak, fp8_peak)
+            line["sweep"] = sweep(args.seed, hbm_peak, fp8_peak,
+                                  tiles=tuple(int(x) for x in args.sweep_tiles.split(",")))
             line["sweep_fp8_peak_tflops"] = fp8_peak
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -19,14 +19,14 @@ struct TileChoice {
 
 constexpr TileChoice kAutotuneTable[] = {
     {256, 16},
-    {512, 32},
-    {INT64_MAX, 64},
+    {2048, 64},
+    {INT64_MAX, 128},
 };
 
 inline int autotune_tile_n(int64_t num_tokens) {
   for (const TileChoice& c : kAutotuneTable)
     if (num_tokens <= c.max_tokens) return c.tile_n;
-  return 64;
+  return 128;
 }
 
 }  // namespace fmoe

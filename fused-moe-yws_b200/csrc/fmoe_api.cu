@@ -82,11 +82,20 @@ int validate(const fmoe_problem* p) {
     return fail(FMOE_ERR_VALUE,
                 "intermediate_size must be a positive multiple of 128 (<= 16384)");
   if (p->tile_n != 0 && !gemm_bn_supported(p->tile_n))
-    return fail(FMOE_ERR_VALUE, "tile_n must be 0 or one of 16, 32, 64");
+    return fail(FMOE_ERR_VALUE, "tile_n must be 0 or one of 16, 32, 64, 128");
+  if (p->tile_n == 128 && p->hidden_size % 256 != 0)
+    return fail(FMOE_ERR_VALUE, "tile_n 128 needs hidden_size to be a multiple of 256");
   const WorkspaceLayout L = make_layout(to_geometry(*p));
   if (L.row_cap * (int64_t)p->hidden_size >= ((int64_t)1 << 40))
     return fail(FMOE_ERR_VALUE, "problem too large for the row-permuted workspace");
   return FMOE_OK;
+}
+
+// Token tile of a call: the caller's choice, else the committed table; the throughput
+// family (128) needs GEMM2's 256-row weight tiles to divide hidden_size.
+int tile_n_of(const fmoe_problem* p) {
+  const int bn = p->tile_n != 0 ? p->tile_n : autotune_tile_n(p->num_tokens);
+  return bn == 128 && p->hidden_size % 256 != 0 ? 64 : bn;
 }
 
 bool aligned(const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; }
@@ -261,7 +270,8 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   v = carve(p, workspace, workspace_bytes, &c);
   if (v != FMOE_OK) return v;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-  const int bn = p->tile_n ? p->tile_n : autotune_tile_n(p->num_tokens);
+  const int bn = tile_n_of(p);
+  const bool tm = bn == 128;  // throughput family: token rows on the MMA M side
   const int64_t T = p->num_tokens;
   const int H = p->hidden_size, I = p->intermediate_size, EL = p->num_local_experts;
 
@@ -336,15 +346,23 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   g.w_scale = t->gemm1_weights_scale;
   g.act_scale = sa.a_scale;
   int64_t bound = c.L.max_chunks * (int64_t)g.m_tiles;
-  FMOE_CUDA_TRY(launch_gemm1(bn, m_w13, m_a, g, (int)(bound < sms ? bound : sms), stream));
+  const int grid1 = (int)(bound < sms ? bound : sms);
+  if (tm)
+    FMOE_CUDA_TRY(launch_gemm1_tm(m_a, m_w13, g, grid1, stream));
+  else
+    FMOE_CUDA_TRY(launch_gemm1(bn, m_w13, m_a, g, grid1, stream));
   if ((v = mark_stage(3, stream)) != FMOE_OK) return v;
 
-  g.m_tiles = H / kBlock;
+  g.m_tiles = tm ? H / 256 : H / kBlock;
   g.k_steps = I / kBlock;
   g.w_scale = t->gemm2_weights_scale;
   g.act_scale = g.c_scale;
   bound = c.L.max_chunks * (int64_t)g.m_tiles;
-  FMOE_CUDA_TRY(launch_gemm2(bn, m_w2, m_cq, g, (int)(bound < sms ? bound : sms), stream));
+  const int grid2 = (int)(bound < sms ? bound : sms);
+  if (tm)
+    FMOE_CUDA_TRY(launch_gemm2_tm(m_cq, m_w2, g, grid2, stream));
+  else
+    FMOE_CUDA_TRY(launch_gemm2(bn, m_w2, m_cq, g, grid2, stream));
   if ((v = mark_stage(4, stream)) != FMOE_OK) return v;
 
   CombineArgs ca;
@@ -398,7 +416,7 @@ extern "C" int fmoe_route(const fmoe_problem* p, const float* routing_logits,
   v = carve(p, workspace, workspace_bytes, &c);
   if (v != FMOE_OK) return v;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-  const int bn = p->tile_n ? p->tile_n : autotune_tile_n(p->num_tokens);
+  const int bn = tile_n_of(p);
   v = launch_route(p, c, routing_logits, routing_bias, bn, stream);
   if (v != FMOE_OK) return v;
   const size_t n = (size_t)p->num_tokens * p->top_k;

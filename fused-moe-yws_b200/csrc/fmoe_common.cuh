@@ -31,7 +31,7 @@ enum MetaSlot : int {
 constexpr int kBlock = 128;        // FP8 block-scale granularity
 constexpr int kRowAlign = 16;      // expert row segments padded to the MMA N granularity
 constexpr int kRouteTokensPerCta = 16;  // one warp per token in the routing kernel
-constexpr int kMaxBN = 64;         // largest token tile (MMA N) the GEMMs use
+constexpr int kMaxBN = 128;        // largest token tile (rows per chunk) the GEMMs use
 constexpr int kMaxLocalExperts = 256;  // experts one call may own (all 8 DS-V3 slices)
 constexpr int kMaxSms = 160;       // upper bound on SMs per GPU for split-K scratch sizing
 constexpr int kTileCounters = kMaxSms;  // stream-K arrival counters, one per CTA

@@ -106,6 +106,11 @@ cudaError_t launch_gemm1(int bn, const CUtensorMap& w13_map, const CUtensorMap& 
                          const GemmArgs& args, int grid, cudaStream_t stream);
 cudaError_t launch_gemm2(int bn, const CUtensorMap& w2_map, const CUtensorMap& cq_map,
                          const GemmArgs& args, int grid, cudaStream_t stream);
+// Throughput family (gemm_sm100_tm.cu): 128 token rows on the MMA M side; tile_n 128.
+cudaError_t launch_gemm1_tm(const CUtensorMap& a_map, const CUtensorMap& w13_map,
+                            const GemmArgs& args, int grid, cudaStream_t stream);
+cudaError_t launch_gemm2_tm(const CUtensorMap& cq_map, const CUtensorMap& w2_map,
+                            const GemmArgs& args, int grid, cudaStream_t stream);
 bool gemm_bn_supported(int bn);
 void set_last_error(const std::string& msg);  // message returned by fmoe_last_error()
 size_t gemm_partial_bytes();

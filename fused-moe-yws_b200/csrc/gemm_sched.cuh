@@ -1,0 +1,68 @@
+// gemm_sched.cuh -- work schedule shared by the grouped GEMM kernels: which tiles and
+// K-step ranges each persistent CTA processes.
+#pragma once
+
+#include <cstdint>
+
+namespace fmoe {
+
+constexpr int kMaxKSteps = 128;  // H/128 and I/128 are validated <= 128
+
+// Stream-K work split: the launch's work is num_tiles x KS K-steps, CTA c owns the
+// contiguous global step range [start(c), start(c+1)). Ranges are cut at tile boundaries
+// into segments; a segment that does not cover its whole tile is a partial.
+struct StreamK {
+  int64_t W;  // total K-steps
+  int G;      // CTAs
+  __device__ __forceinline__ int64_t start(int c) const { return (int64_t)c * W / G; }
+  // the CTA whose range contains global step g
+  __device__ __forceinline__ int cta_of(int64_t g) const {
+    return (int)(((g + 1) * G + W - 1) / W) - 1;
+  }
+};
+
+// Per-CTA work sequence: whole tiles round-robin over the CTAs for all but the last one
+// to two waves ("data parallel": CTAs that run together work on neighbouring tiles, so an
+// expert's weight tiles are shared through L2 by its chunks), then the remaining tiles
+// split by stream-K so every CTA ends at the same time. Every role walks the same sequence.
+struct Schedule {
+  int KS, G, cta;
+  int dp_tiles;  // whole-tile prefix, a multiple of G
+  StreamK sk;    // over the remaining tiles, in K-step units
+  int64_t g, g_end;
+  int dp_next;
+
+  __device__ __forceinline__ Schedule(int num_tiles, int ks, int grid, int c) {
+    KS = ks;
+    G = grid;
+    cta = c;
+    dp_tiles = num_tiles > 2 * G ? (num_tiles / G - 1) * G : 0;
+    sk.W = (int64_t)(num_tiles - dp_tiles) * KS;
+    sk.G = G;
+    g = sk.start(c);
+    g_end = sk.start(c + 1);
+    dp_next = c;
+  }
+  // next segment: tile index, K-step range [k0, k1); false when done
+  __device__ __forceinline__ bool next(int& tile, int& k0, int& k1) {
+    if (dp_next < dp_tiles) {
+      tile = dp_next;
+      k0 = 0;
+      k1 = KS;
+      dp_next += G;
+      return true;
+    }
+    if (g < g_end) {
+      const int64_t lt = g / KS;
+      k0 = (int)(g % KS);
+      k1 = (int)((int64_t)KS < k0 + (g_end - g) ? KS : k0 + (g_end - g));
+      g += k1 - k0;
+      tile = dp_tiles + (int)lt;
+      return true;
+    }
+    return false;
+  }
+  __device__ __forceinline__ int64_t sk_begin() const { return sk.start(cta); }
+};
+
+}  // namespace fmoe

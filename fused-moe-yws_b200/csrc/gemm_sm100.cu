@@ -11,15 +11,15 @@
 // byte is thus read once per chunk, which is what the bandwidth-bound regime needs, and
 // a ragged expert wastes at most 15 MMA columns instead of a 128-row M tile.
 //
-// GEMM1 (+SwiGLU): tile = 64 gate rows [i0, i0+64) and the matching 64 up rows
-//   [I+i0, I+i0+64) of W13 (kernel.cu:829-831 pairs G1[:, c] with G1[:, I + c]).
+// GEMM1 (+SwiGLU): tile = 128 gate rows [i0, i0+128) and the matching 128 up rows
+//   [I+i0, I+i0+128) of W13 (kernel.cu:829-831 pairs G1[:, c] with G1[:, I + c]).
 //   Per K block kb (128): D = W13_tile . A_chunk^T in TMEM; epilogue warps add
 //   D * w_scale[row block, kb] * a_scale[token, kb] into fp32 registers. The tile
 //   epilogue forms C = x1 * silu(x2) and writes it as an FP8 hi/lo pair on one
-//   per-(token, 64-column) scale: C ~ scale * (hi + lo), relative error ~2^-8.
-// GEMM2: tile = 128 rows h of W2. Per 64-column C block j: D = W2[:, 64j:64j+64] .
+//   per-(token, 128-column) scale: C ~ scale * (hi + lo), relative error ~2^-8.
+// GEMM2: tile = 128 rows h of W2. Per 128-column C block j: D = W2[:, 128j:128j+128] .
 //   hi_j^T + W2[...] . lo_j^T (both into the same accumulator: same scale), promoted
-//   with w2_scale[h block, j/2] * c_scale[token, j]. Epilogue writes
+//   with w2_scale[h block, j] * c_scale[token, j]. Epilogue writes
 //   bf16(D * routing_weight) per routed row for the deterministic combine.
 //
 // Warp roles (320 threads, one CTA per SM, persistent over the tile list):
@@ -33,6 +33,7 @@
 
 #include "fmoe_common.cuh"
 #include "fmoe_kernels.cuh"
+#include "gemm_sched.cuh"
 #include "sm100.cuh"
 
 namespace fmoe {
@@ -43,7 +44,6 @@ namespace {
 
 constexpr int kThreads = 320;
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in dynamic shared memory per CTA
-constexpr int kMaxKSteps = 128;     // H/128 and I/128 are validated <= 128
 constexpr int kEpiThreads = 256;    // warps 2..9
 constexpr int kBarAll = 3;          // named barrier id over all epilogue warps
 
@@ -63,7 +63,7 @@ struct Cfg {
   static constexpr int kNBuf = kNBufRaw > 8 ? 8 : kNBufRaw;   // accumulator ring depth
   static constexpr int kExBytes = kG1 ? 2 * 128 * (HB + 1) * 4 : 0;  // SwiGLU staging
   static_assert(!kG1 || HB * 4 <= 128, "SwiGLU quantisation maps 4 threads per token column");
-  static constexpr int kWscBytes = 2 * kMaxKSteps * 4;        // [gate/up][k step]
+  static constexpr int kWscBytes = 2 * 2 * kMaxKSteps * 4;    // [slot][gate/up][k step]
   static constexpr int kSlotBytes = BN * 4;                   // act scales of one K step
   static constexpr int kMaxSlots = 16 + 8 + 2;
   static constexpr int kBarBytes = 1024;
@@ -79,7 +79,7 @@ struct Cfg {
   static constexpr int kPartialFloats = kAcc * 128 * BN;      // one split-K partial tile
   static_assert(kStages >= 2, "not enough shared memory for a 2-stage pipeline");
   static_assert(kSmemBytes <= kSmemLimit, "shared memory budget");
-  static_assert((16 + 16 + 8 + 8 + 2 * kMaxSlots + 3) * 8 <= kBarBytes, "barrier area");
+  static_assert((16 + 16 + 8 + 8 + 4 + 2 * kMaxSlots + 3) * 8 <= kBarBytes, "barrier area");
   static_assert(kNBuf >= 2, "need at least two accumulator buffers");
 };
 
@@ -89,63 +89,6 @@ __device__ __forceinline__ void set_error(int* err, volatile int* abort_flag, in
   atomicOr(err, code);
   *abort_flag = 1;
 }
-
-// Stream-K work split: the launch's work is num_tiles x KS K-steps, CTA c owns the
-// contiguous global step range [start(c), start(c+1)). Ranges are cut at tile boundaries
-// into segments; a segment that does not cover its whole tile is a partial.
-struct StreamK {
-  int64_t W;  // total K-steps
-  int G;      // CTAs
-  __device__ __forceinline__ int64_t start(int c) const { return (int64_t)c * W / G; }
-  // the CTA whose range contains global step g
-  __device__ __forceinline__ int cta_of(int64_t g) const {
-    return (int)(((g + 1) * G + W - 1) / W) - 1;
-  }
-};
-
-// Per-CTA work sequence: whole tiles round-robin over the CTAs for all but the last one
-// to two waves ("data parallel": CTAs that run together work on neighbouring tiles, so an
-// expert's weight tiles are shared through L2 by its chunks), then the remaining tiles
-// split by stream-K so every CTA ends at the same time. Every role walks the same sequence.
-struct Schedule {
-  int KS, G, cta;
-  int dp_tiles;  // whole-tile prefix, a multiple of G
-  StreamK sk;    // over the remaining tiles, in K-step units
-  int64_t g, g_end;
-  int dp_next;
-
-  __device__ __forceinline__ Schedule(int num_tiles, int ks, int grid, int c) {
-    KS = ks;
-    G = grid;
-    cta = c;
-    dp_tiles = num_tiles > 2 * G ? (num_tiles / G - 1) * G : 0;
-    sk.W = (int64_t)(num_tiles - dp_tiles) * KS;
-    sk.G = G;
-    g = sk.start(c);
-    g_end = sk.start(c + 1);
-    dp_next = c;
-  }
-  // next segment: tile index, K-step range [k0, k1); false when done
-  __device__ __forceinline__ bool next(int& tile, int& k0, int& k1) {
-    if (dp_next < dp_tiles) {
-      tile = dp_next;
-      k0 = 0;
-      k1 = KS;
-      dp_next += G;
-      return true;
-    }
-    if (g < g_end) {
-      const int64_t lt = g / KS;
-      k0 = (int)(g % KS);
-      k1 = (int)((int64_t)KS < k0 + (g_end - g) ? KS : k0 + (g_end - g));
-      g += k1 - k0;
-      tile = dp_tiles + (int)lt;
-      return true;
-    }
-    return false;
-  }
-  __device__ __forceinline__ int64_t sk_begin() const { return sk.start(cta); }
-};
 
 // Promote one accumulator: acc[j] += D[row, col_j] * scale_j * sw for this thread's
 // half of the token columns (only column chunks below ncols are read).
@@ -244,7 +187,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = bars + 16;           // [S]   MMA -> TMA
   uint64_t* tfull = bars + 32;           // [NB]  MMA -> epilogue
   uint64_t* tempty = bars + 40;          // [NB]  epilogue -> MMA
-  uint64_t* sfull = bars + 48;           // [SR]  scale ring, TMA -> epilogue
+  uint64_t* wfull = bars + 48;           // [2]   weight-scale rows, producer -> epilogue
+  uint64_t* wempty = bars + 50;          // [2]   epilogue -> producer
+  uint64_t* sfull = bars + 52;           // [SR]  scale ring, TMA -> epilogue
   uint64_t* sempty = sfull + C::kMaxSlots;  // [SR] epilogue -> TMA
   uint64_t* mma_done = sempty + C::kMaxSlots;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
@@ -264,6 +209,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int r = 0; r < SR; ++r) {
       mbar_init(&sfull[r], 1);
       mbar_init(&sempty[r], 8);
+    }
+    for (int r = 0; r < 2; ++r) {
+      mbar_init(&wfull[r], 32);
+      mbar_init(&wempty[r], 8);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -290,16 +239,45 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
-      const uint64_t pol_w = policy_evict_first();  // weights: streamed once
-      const uint64_t pol_a = policy_evict_last();   // token tiles: re-read by every m tile
-      int it = 0;
-      bool ok = true;
-      Schedule sched(num_tiles, KS, (int)gridDim.x, cta);
-      int tile, k0, k1;
-      while (ok && sched.next(tile, k0, k1)) {
-        const Chunk ch = args.chunks[tile / args.m_tiles];
-        const int m = tile % args.m_tiles;
+    // The whole warp stages each tile's weight block scales (one W2 row, or the gate and
+    // up rows of W13) into a 2-slot shared ring; lane 0 alone issues the copies.
+    const uint64_t pol_w = policy_evict_first();  // weights: streamed once
+    const uint64_t pol_a = policy_evict_last();   // token tiles: re-read by every m tile
+    int it = 0, wseg = 0;
+    bool ok = true;
+    Schedule sched(num_tiles, KS, (int)gridDim.x, cta);
+    int tile, k0, k1;
+    while (ok && sched.next(tile, k0, k1)) {
+      const Chunk ch = args.chunks[tile / args.m_tiles];
+      const int m = tile % args.m_tiles;
+      {
+        const int ws = wseg & 1;
+        bool w_ok = true;
+        if (lane == 0) w_ok = mbar_wait(&wempty[ws], ((wseg >> 1) & 1) ^ 1, abort_flag);
+        if (!__shfl_sync(0xffffffffu, w_ok, 0)) {
+          ok = false;
+          break;
+        }
+        const int kbh = (kG1 ? args.H : args.I) / kBlock;
+        const float* g;
+        const float* u;
+        if constexpr (kG1) {
+          const int nb2 = 2 * args.I / kBlock;
+          g = args.w_scale + ((int64_t)ch.expert * nb2 + m) * kbh;
+          u = args.w_scale + ((int64_t)ch.expert * nb2 + args.I / kBlock + m) * kbh;
+        } else {
+          g = args.w_scale + ((int64_t)ch.expert * (args.H / kBlock) + m) * kbh;
+          u = g;
+        }
+        float* dst = wsc + ws * 2 * kMaxKSteps;
+        for (int i = lane; i < kbh; i += 32) {
+          dst[i] = __ldg(g + i);
+          if constexpr (kG1) dst[kMaxKSteps + i] = __ldg(u + i);
+        }
+        mbar_arrive(&wfull[ws]);  // every lane: its stores are released by its own arrive
+        ++wseg;
+      }
+      if (lane == 0) {
         const float* asrc = args.act_scale + ch.row0;
         for (int ks = k0; ks < k1; ++ks, ++it) {
           const int s = it % S, slot = it % SR;
@@ -328,6 +306,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                        &sfull[slot]);
         }
       }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
+    if (lane == 0) {
       if (!ok) set_error(args.err, abort_flag, kErrTimeoutProducer);
       // drain: every issued copy must land before the CTA's shared memory is released
       static const int zero = 0;
@@ -402,7 +383,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int bar_half = 1 + half;    // named barrier of the 4 warps of this half
     float acc_g[HB];
     float acc_u[kG1 ? HB : 1];
-    int it = 0;
+    int it = 0, wseg = 0;
     bool ok = true;
     Schedule sched(num_tiles, KS, (int)gridDim.x, cta);
     int tile, k0, k1;
@@ -410,24 +391,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const Chunk ch = args.chunks[tile / args.m_tiles];
       const int m = tile % args.m_tiles;
       const int ncols = ch.ncols;
-      // weight block scales of this tile (one row for W2, gate and up rows for W13)
-      named_bar(kBarAll, kEpiThreads);
-      {
-        const int kbh = (kG1 ? args.H : args.I) / kBlock;
-        const float* g;
-        const float* u;
-        if constexpr (kG1) {
-          const int nb2 = 2 * args.I / kBlock;
-          g = args.w_scale + ((int64_t)ch.expert * nb2 + m) * kbh;
-          u = args.w_scale + ((int64_t)ch.expert * nb2 + args.I / kBlock + m) * kbh;
-        } else {
-          g = args.w_scale + ((int64_t)ch.expert * (args.H / kBlock) + m) * kbh;
-          u = g;
-        }
-        for (int i = tid_e; i < 2 * kbh; i += kEpiThreads)
-          wsc[(i >= kbh) * kMaxKSteps + (i % kbh)] = __ldg((i >= kbh ? u : g) + (i % kbh));
-      }
-      named_bar(kBarAll, kEpiThreads);
+      // weight block scales of this tile, staged by the producer warp
+      const int ws = wseg & 1;
+      if (ok && !mbar_wait(&wfull[ws], (wseg >> 1) & 1, abort_flag)) ok = false;
+      const float* wrow = wsc + ws * 2 * kMaxKSteps;
 #pragma unroll
       for (int j = 0; j < HB; ++j) acc_g[j] = 0.0f;
       if constexpr (kG1) {
@@ -446,8 +413,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const float* sa = sring + slot * BN + half * HB;
         const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + b * C::kBufCols + half * HB;
-        promote<HB, CW>(acc_g, tb, sa, wsc[ks], half * HB, ncols);
-        if constexpr (kG1) promote<HB, CW>(acc_u, tb + C::kBNs, sa, wsc[kMaxKSteps + ks], half * HB, ncols);
+        promote<HB, CW>(acc_g, tb, sa, wrow[ks], half * HB, ncols);
+        if constexpr (kG1) promote<HB, CW>(acc_u, tb + C::kBNs, sa, wrow[kMaxKSteps + ks], half * HB, ncols);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
@@ -455,6 +422,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive(&sempty[slot]);
         }
       }
+      // the weight-scale slot is free again once this warp's promotions are done
+      __syncwarp();
+      if (lane == 0 && ok) mbar_arrive(&wempty[ws]);
+      ++wseg;
       // one abort decision for all epilogue warps (nobody waits at a barrier alone)
       if (named_bar_or(kBarAll, kEpiThreads, !ok)) {
         ok = false;
@@ -590,12 +561,12 @@ cudaError_t launch_one(const CUtensorMap& a, const CUtensorMap& b, const GemmArg
 
 }  // namespace
 
-bool gemm_bn_supported(int bn) { return bn == 16 || bn == 32 || bn == 64; }
+bool gemm_bn_supported(int bn) { return bn == 16 || bn == 32 || bn == 64 || bn == 128; }
 
 size_t gemm_partial_bytes() {
   // stream-K: two partial slots per CTA; one partial tile is at most 2 accumulators x 128
-  // rows x 64 columns of fp32 (GEMM1) or 128 x 64 (GEMM2)
-  return (size_t)2 * kMaxSms * 2 * 128 * 64 * sizeof(float);
+  // rows x 64 columns of fp32 (decode GEMM1) or 128 token rows x 256 columns (throughput)
+  return (size_t)2 * kMaxSms * 128 * 256 * sizeof(float);
 }
 
 cudaError_t launch_gemm1(int bn, const CUtensorMap& w13_map, const CUtensorMap& a_map,

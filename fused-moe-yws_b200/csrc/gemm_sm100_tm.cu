@@ -1,0 +1,514 @@
+// gemm_sm100_tm.cu -- throughput ("token-major") family of the grouped FP8 GEMMs, used
+// when experts receive many rows (large T, skewed routing, the expert-parallel layer).
+//
+// Same operator as gemm_sm100.cu (reference solution/cuda/kernel.cu:1006-1199 and the
+// CUTLASS grouped GEMMs at :73-115 / :1221-1417), other orientation: the MMA M side is
+// 128 routed token rows of one expert, the N side is 256 weight rows. Per 128-K block one
+// tcgen05.mma M128 x N256 x K128 (four K = 32 instructions) fills a 256-column TMEM
+// accumulator; an epilogue thread owns one token row, so the block-scale promotion is a
+// single FMA per element with a per-thread scalar (token scale x weight-block scale).
+//   GEMM1: N = 128 gate rows [128 m, 128 m + 128) + the matching 128 up rows of W13; the
+//          thread holding token row r and C columns [32 j, 32 j + 32) reads gate columns
+//          32 j.. and up columns 128 + 32 j..: SwiGLU is thread-local; the per-(token,
+//          128-column) amax is combined across the 4 column slices through shared memory.
+//   GEMM2: N = 256 rows of W2 (two 128-row scale blocks); the thread owns 64 consecutive
+//          output columns of its token row and stores them as 128 contiguous bytes.
+// Warps: 0 TMA producer (also stages each tile's weight-scale rows into a 2-slot ring),
+// 1 TMEM allocator + MMA issuer, 2..17 epilogue (TMEM lane quadrant = warp % 4, column
+// slice = (warp - 2) / 4). Two 256-column TMEM accumulators let the MMA of K block kb+1
+// overlap the promotion of kb. The schedule (data-parallel waves, stream-K tail), bounded
+// waits, abort protocol and error reporting are those of gemm_sm100.cu.
+#include <cuda_fp8.h>
+
+#include "fmoe_common.cuh"
+#include "fmoe_kernels.cuh"
+#include "gemm_sched.cuh"
+#include "sm100.cuh"
+
+namespace fmoe {
+
+using namespace sm100;
+
+namespace {
+
+constexpr int kTmThreads = 576;     // 18 warps
+constexpr int kTmEpiThreads = 512;  // warps 2..17
+constexpr int kTmBarAll = 1;        // named barrier over the epilogue warps
+constexpr int kTmSmemLimit = 232448;
+
+template <bool kG1>
+struct TmCfg {
+  static constexpr int kABytes = kG1 ? 128 * 128 : 2 * 128 * 128;  // tokens (G2: hi + lo)
+  static constexpr int kBBytes = 256 * 128;                        // 256 weight rows
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kNBuf = 2;                                  // 2 x 256 TMEM columns
+  static constexpr int kSlotBytes = 128 * 4;                       // token scales, one K step
+  static constexpr int kAxBytes = kG1 ? 4 * 128 * 4 : 0;           // amax exchange
+  static constexpr int kWscBytes = 2 * 2 * kMaxKSteps * 4;         // [slot][row 0/1][k step]
+  static constexpr int kMaxSlots = 16 + 2 + 2;
+  static constexpr int kBarBytes = 1024;
+  static constexpr int kFixedMax =
+      1024 + kAxBytes + kWscBytes + kMaxSlots * kSlotBytes + kBarBytes + 64;
+  static constexpr int kStagesRaw = (kTmSmemLimit - kFixedMax) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 16 ? 16 : kStagesRaw;
+  static constexpr int kSlots = kStages + kNBuf + 2;
+  static constexpr int kFixed = 1024 + kAxBytes + kWscBytes + kSlots * kSlotBytes + kBarBytes + 64;
+  static constexpr int kSmemBytes = kFixed + kStages * kStageBytes;
+  static constexpr int kPartialFloats = 128 * 256;
+  static_assert(kStages >= 2, "pipeline depth");
+  static_assert(kSmemBytes <= kTmSmemLimit, "shared memory budget");
+  static_assert((16 + 16 + 2 + 2 + 4 + 2 * kMaxSlots + 3) * 8 <= kBarBytes, "barrier area");
+};
+
+__device__ __forceinline__ float silu_tm(float x) { return x / (1.0f + __expf(-x)); }
+
+template <int N>
+__device__ __forceinline__ void promote_tm(float (&acc)[N], uint32_t taddr, float s) {
+#pragma unroll
+  for (int c = 0; c < N / 16; ++c) {
+    uint32_t v[16];
+    tmem_ld_32x32b<16>(taddr + c * 16, v);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[c * 16 + i] = fmaf(__uint_as_float(v[i]), s, acc[c * 16 + i]);
+  }
+}
+
+template <int N>
+__device__ __forceinline__ void store_vec(float* dst, const float (&v)[N]) {
+#pragma unroll
+  for (int j = 0; j < N; j += 4)
+    *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+}
+
+// Sum of a tile's stream-K contributions (partials in [row][256] layout), in K order; CTAs
+// with an empty range contribute nothing. Partials come from other CTAs: L2-coherent loads.
+template <int N>
+__device__ __forceinline__ void sum_tm(float (&acc)[N], const float* partials, int64_t off,
+                                       const StreamK& sk, int64_t tile_begin, int cf, int cl) {
+#pragma unroll
+  for (int j = 0; j < N; ++j) acc[j] = 0.0f;
+  for (int c = cf; c <= cl; ++c) {
+    if (sk.start(c) == sk.start(c + 1)) continue;
+    const int slot = sk.start(c) >= tile_begin ? 0 : 1;
+    const float* p = partials + (int64_t)(2 * c + slot) * (128 * 256) + off;
+#pragma unroll
+    for (int j = 0; j < N; j += 4) {
+      const float4 x = __ldcg(reinterpret_cast<const float4*>(p + j));
+      acc[j] += x.x;
+      acc[j + 1] += x.y;
+      acc[j + 2] += x.z;
+      acc[j + 3] += x.w;
+    }
+  }
+}
+
+template <bool kG1>
+__global__ void __launch_bounds__(kTmThreads, 1)
+    grouped_gemm_tm_kernel(const __grid_constant__ CUtensorMap tmA,
+                           const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+  using C = TmCfg<kG1>;
+  constexpr int S = C::kStages, NB = C::kNBuf, SR = C::kSlots;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint8_t* fixed = smem + S * C::kStageBytes;
+  float* ax = reinterpret_cast<float*>(fixed);
+  float* wsc = reinterpret_cast<float*>(fixed + C::kAxBytes);
+  float* sring = reinterpret_cast<float*>(fixed + C::kAxBytes + C::kWscBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(fixed + C::kAxBytes + C::kWscBytes +
+                                               SR * C::kSlotBytes);
+  uint64_t* full = bars;          // [S]  TMA -> MMA
+  uint64_t* empty = bars + 16;    // [S]  MMA -> TMA
+  uint64_t* tfull = bars + 32;    // [2]  MMA -> epilogue
+  uint64_t* tempty = bars + 34;   // [2]  epilogue -> MMA
+  uint64_t* wfull = bars + 36;    // [2]  weight-scale rows, producer -> epilogue
+  uint64_t* wempty = bars + 38;   // [2]  epilogue -> producer
+  uint64_t* sfull = bars + 40;    // [SR] token-scale ring, TMA -> epilogue
+  uint64_t* sempty = sfull + C::kMaxSlots;
+  uint64_t* mma_done = sempty + C::kMaxSlots;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(mma_done + 2);
+  volatile int* last_flag = abort_flag + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < NB; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 16);
+    }
+    for (int r = 0; r < SR; ++r) {
+      mbar_init(&sfull[r], 1);
+      mbar_init(&sempty[r], 16);
+    }
+    for (int r = 0; r < 2; ++r) {
+      mbar_init(&wfull[r], 32);
+      mbar_init(&wempty[r], 16);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait();
+  pdl_trigger();
+
+  const int num_tiles = args.meta[kMetaNumChunks] * args.m_tiles;
+  const int KS = args.k_steps;
+  const int cta = (int)blockIdx.x;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    // The whole warp stages each tile's weight block scales into a 2-slot shared ring;
+    // lane 0 alone issues the copies.
+    const uint64_t pol_w = policy_evict_first();
+    const uint64_t pol_a = policy_evict_last();
+    int it = 0, wseg = 0;
+    bool ok = true;
+    Schedule sched(num_tiles, KS, (int)gridDim.x, cta);
+    int tile, k0, k1;
+    while (ok && sched.next(tile, k0, k1)) {
+      const Chunk ch = args.chunks[tile / args.m_tiles];
+      const int m = tile % args.m_tiles;
+      {
+        // GEMM1: gate block m and up block I/128 + m (H/128 values each);
+        // GEMM2: h blocks 2 m and 2 m + 1 (I/128 values each)
+        const int ws = wseg & 1;
+        bool w_ok = true;
+        if (lane == 0) w_ok = mbar_wait(&wempty[ws], ((wseg >> 1) & 1) ^ 1, abort_flag);
+        if (!__shfl_sync(0xffffffffu, w_ok, 0)) {
+          ok = false;
+          break;
+        }
+        const float* g;
+        const float* u;
+        int n;
+        if constexpr (kG1) {
+          const int nb2 = 2 * args.I / kBlock;
+          n = args.H / kBlock;
+          g = args.w_scale + ((int64_t)ch.expert * nb2 + m) * n;
+          u = args.w_scale + ((int64_t)ch.expert * nb2 + args.I / kBlock + m) * n;
+        } else {
+          n = args.I / kBlock;
+          g = args.w_scale + ((int64_t)ch.expert * (args.H / kBlock) + 2 * m) * n;
+          u = g + n;
+        }
+        float* dst = wsc + ws * 2 * kMaxKSteps;
+        for (int i = lane; i < n; i += 32) {
+          dst[i] = __ldg(g + i);
+          dst[kMaxKSteps + i] = __ldg(u + i);
+        }
+        mbar_arrive(&wfull[ws]);  // every lane: its stores are released by its own arrive
+        ++wseg;
+      }
+      if (lane == 0) {
+        const float* asrc = args.act_scale + ch.row0;
+        for (int ks = k0; ks < k1; ++ks, ++it) {
+          const int s = it % S, slot = it % SR;
+          if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, abort_flag) ||
+              !mbar_wait(&sempty[slot], ((it / SR) & 1) ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = stages + s * C::kStageBytes;
+          uint8_t* sb = sa + C::kABytes;
+          mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+          if constexpr (kG1) {
+            tma_load_2d(sa, &tmA, &full[s], ks * 128, ch.row0, pol_a);
+            const int wrow = ch.expert * 2 * args.I + m * 128;
+            tma_load_2d(sb, &tmB, &full[s], ks * 128, wrow, pol_w);
+            tma_load_2d(sb + 128 * 128, &tmB, &full[s], ks * 128, wrow + args.I, pol_w);
+          } else {
+            tma_load_2d(sa, &tmA, &full[s], ks * 256, ch.row0, pol_a);                    // hi
+            tma_load_2d(sa + 128 * 128, &tmA, &full[s], ks * 256 + 128, ch.row0, pol_a);  // lo
+            const int wrow = ch.expert * args.H + m * 256;
+            tma_load_2d(sb, &tmB, &full[s], ks * 128, wrow, pol_w);
+            tma_load_2d(sb + 128 * 128, &tmB, &full[s], ks * 128, wrow + 128, pol_w);
+          }
+          mbar_arrive_expect_tx(&sfull[slot], ch.ncols * 4);
+          bulk_load_1d(sring + slot * 128, asrc + (int64_t)ks * args.row_cap, ch.ncols * 4,
+                       &sfull[slot]);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
+    if (lane == 0) {
+      if (!ok) {
+        atomicOr(args.err, kErrTimeoutProducer);
+        *abort_flag = 1;
+      }
+      // drain: every issued copy must land before the CTA's shared memory is released
+      static const int zero = 0;
+      for (int j = it > S ? it - S : 0; j < it; ++j) mbar_wait(&full[j % S], (j / S) & 1, &zero);
+      for (int j = it > SR ? it - SR : 0; j < it; ++j)
+        mbar_wait(&sfull[j % SR], (j / SR) & 1, &zero);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      const uint32_t idesc = idesc_e4m3_f32(128, 256);
+      Schedule sched(num_tiles, KS, (int)gridDim.x, cta);
+      int tile, k0, k1;
+      while (ok && sched.next(tile, k0, k1)) {
+        for (int ks = k0; ks < k1; ++ks, ++it) {
+          const int b = it % NB, use = it / NB;
+          if (!mbar_wait(&tempty[b], (use & 1) ^ 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const int s = it % S;
+          if (!mbar_wait(&full[s], (it / S) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_addr(stages + s * C::kStageBytes);
+          const uint32_t d = tmem + b * 256;
+          const uint64_t bd = smem_desc_kmajor(sa + C::kABytes, 128);
+          if constexpr (kG1) {
+            const uint64_t ad = smem_desc_kmajor(sa, 128);
+#pragma unroll
+            for (int sub = 0; sub < 4; ++sub) mma_f8f6f4(d, ad + 2 * sub, bd + 2 * sub, idesc, sub > 0);
+          } else {
+            // hi and lo parts of the C block share one scale -> one accumulator
+            const uint64_t ah = smem_desc_kmajor(sa, 128);
+            const uint64_t al = smem_desc_kmajor(sa + 128 * 128, 128);
+#pragma unroll
+            for (int sub = 0; sub < 4; ++sub) mma_f8f6f4(d, ah + 2 * sub, bd + 2 * sub, idesc, sub > 0);
+#pragma unroll
+            for (int sub = 0; sub < 4; ++sub) mma_f8f6f4(d, al + 2 * sub, bd + 2 * sub, idesc, 1);
+          }
+          tc_commit(&empty[s]);
+          tc_commit(&tfull[b]);
+        }
+      }
+      if (!ok) {
+        atomicOr(args.err, kErrTimeoutMma);
+        *abort_flag = 1;
+      }
+      // all issued MMAs must retire before TMEM is released
+      static const int zero = 0;
+      tc_commit(mma_done);
+      mbar_wait(mma_done, 0, &zero);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int ew = warp - 2;        // 0..15
+    const int q = warp & 3;         // TMEM lane quadrant = token rows 32 q .. 32 q + 31
+    const int j = ew >> 2;          // column slice 0..3
+    const int tid_e = ew * 32 + lane;
+    const int row = q * 32 + lane;  // token row inside the tile
+    constexpr int NA = kG1 ? 32 : 64;
+    float acc[NA];
+    float acc_u[kG1 ? 32 : 1];
+    int it = 0, wseg = 0;
+    bool ok = true;
+    Schedule sched(num_tiles, KS, (int)gridDim.x, cta);
+    int tile, k0, k1;
+    while (sched.next(tile, k0, k1)) {
+      const Chunk ch = args.chunks[tile / args.m_tiles];
+      const int m = tile % args.m_tiles;
+      // weight-scale rows of this tile, staged by the producer into the 2-slot ring
+      const int ws = wseg & 1;
+      if (ok && !mbar_wait(&wfull[ws], (wseg >> 1) & 1, abort_flag)) ok = false;
+      const float* wrow = wsc + ws * 2 * kMaxKSteps;
+#pragma unroll
+      for (int i = 0; i < NA; ++i) acc[i] = 0.0f;
+      if constexpr (kG1) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc_u[i] = 0.0f;
+      }
+      for (int ks = k0; ks < k1; ++ks, ++it) {
+        const int b = it % NB, use = it / NB;
+        const int slot = it % SR, suse = it / SR;
+        if (!ok) continue;
+        if (!mbar_wait(&sfull[slot], suse & 1, abort_flag) ||
+            !mbar_wait(&tfull[b], use & 1, abort_flag)) {
+          ok = false;
+          continue;
+        }
+        tc_fence_after();
+        const float st = sring[slot * 128 + row];  // token scale (rows >= ncols: unused)
+        const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + b * 256;
+        if constexpr (kG1) {
+          promote_tm<32>(acc, tb + 32 * j, st * wrow[ks]);
+          promote_tm<32>(acc_u, tb + 128 + 32 * j, st * wrow[kMaxKSteps + ks]);
+        } else {
+          promote_tm<64>(acc, tb + 64 * j, st * wrow[(j >= 2) * kMaxKSteps + ks]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&tempty[b]);
+          mbar_arrive(&sempty[slot]);
+        }
+      }
+      // the weight-scale slot is free again once this warp's promotions are done
+      __syncwarp();
+      if (lane == 0 && ok) mbar_arrive(&wempty[ws]);
+      ++wseg;
+      // one abort decision for all epilogue warps (nobody waits at a barrier alone)
+      if (named_bar_or(kTmBarAll, kTmEpiThreads, !ok)) {
+        ok = false;
+        break;
+      }
+      // ---- stream-K partial tiles ([row][256] fp32), finished by the last contributor ----
+      if (k0 != 0 || k1 != KS) {
+        const StreamK& sk = sched.sk;
+        const int64_t tile_begin = (int64_t)(tile - sched.dp_tiles) * KS;
+        const int slot = sched.sk_begin() >= tile_begin ? 0 : 1;
+        float* part = args.partials + (int64_t)(2 * cta + slot) * C::kPartialFloats + row * 256;
+        if constexpr (kG1) {
+          store_vec<32>(part + 32 * j, acc);
+          store_vec<32>(part + 128 + 32 * j, acc_u);
+        } else {
+          store_vec<64>(part + 64 * j, acc);
+        }
+        __threadfence();
+        named_bar(kTmBarAll, kTmEpiThreads);
+        const int cf = sk.cta_of(tile_begin), cl = sk.cta_of(tile_begin + KS - 1);
+        if (tid_e == 0) {
+          const int done = atomicAdd(args.tile_counters + cf, k1 - k0) + (k1 - k0);
+          const bool last = done == KS;
+          if (last) args.tile_counters[cf] = 0;  // ready for the next launch
+          *last_flag = last;
+        }
+        named_bar(kTmBarAll, kTmEpiThreads);
+        if (!*last_flag) continue;
+        __threadfence();
+        if constexpr (kG1) {
+          sum_tm<32>(acc, args.partials, row * 256 + 32 * j, sk, tile_begin, cf, cl);
+          sum_tm<32>(acc_u, args.partials, row * 256 + 128 + 32 * j, sk, tile_begin, cf, cl);
+        } else {
+          sum_tm<64>(acc, args.partials, row * 256 + 64 * j, sk, tile_begin, cf, cl);
+        }
+      }
+
+      const bool real = row < ch.rows;  // rows past the chunk belong to the next expert
+      const int64_t grow = (int64_t)ch.row0 + row;
+      if constexpr (kG1) {
+        // ---- SwiGLU, then FP8 hi/lo on one per-(token, 128-column) scale ----
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          acc[i] = acc[i] * silu_tm(acc_u[i]);
+          amax = fmaxf(amax, fabsf(acc[i]));
+        }
+        ax[j * 128 + row] = amax;
+        named_bar(kTmBarAll, kTmEpiThreads);
+        amax = fmaxf(fmaxf(ax[row], ax[128 + row]), fmaxf(ax[256 + row], ax[384 + row]));
+        if (real) {
+          const float inv = amax > 0.0f ? 448.0f / amax : 0.0f;
+          uint32_t hi[8], lo[8];
+#pragma unroll
+          for (int k = 0; k < 32; k += 4) {
+            float x[4], h[4], l[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) x[u] = acc[k + u] * inv;
+            const __nv_fp8x2_storage_t h01 =
+                __nv_cvt_float2_to_fp8x2(make_float2(x[0], x[1]), __NV_SATFINITE, __NV_E4M3);
+            const __nv_fp8x2_storage_t h23 =
+                __nv_cvt_float2_to_fp8x2(make_float2(x[2], x[3]), __NV_SATFINITE, __NV_E4M3);
+            const __half2_raw hr01 = __nv_cvt_fp8x2_to_halfraw2(h01, __NV_E4M3);
+            const __half2_raw hr23 = __nv_cvt_fp8x2_to_halfraw2(h23, __NV_E4M3);
+            const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&hr01));
+            const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&hr23));
+            h[0] = f01.x; h[1] = f01.y; h[2] = f23.x; h[3] = f23.y;
+#pragma unroll
+            for (int u = 0; u < 4; ++u) l[u] = x[u] - h[u];
+            const __nv_fp8x2_storage_t l01 =
+                __nv_cvt_float2_to_fp8x2(make_float2(l[0], l[1]), __NV_SATFINITE, __NV_E4M3);
+            const __nv_fp8x2_storage_t l23 =
+                __nv_cvt_float2_to_fp8x2(make_float2(l[2], l[3]), __NV_SATFINITE, __NV_E4M3);
+            hi[k / 4] = (uint32_t)h01 | ((uint32_t)h23 << 16);
+            lo[k / 4] = (uint32_t)l01 | ((uint32_t)l23 << 16);
+          }
+          uint8_t* dst = args.cq + grow * (2 * (int64_t)args.I) + m * 256 + j * 32;
+          reinterpret_cast<uint4*>(dst)[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+          reinterpret_cast<uint4*>(dst)[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+          reinterpret_cast<uint4*>(dst + 128)[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+          reinterpret_cast<uint4*>(dst + 128)[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+          if (j == 0) args.c_scale[(int64_t)m * args.row_cap + grow] = amax / 448.0f;
+        }
+        named_bar(kTmBarAll, kTmEpiThreads);  // ax is reused by the next tile
+      } else {
+        // ---- weighted expert output: 64 consecutive bf16 of this token row ----
+        if (real) {
+          const float w = __ldg(args.row_w + grow);
+          uint4* dst = reinterpret_cast<uint4*>(args.ow + grow * args.H + m * 256 + 64 * j);
+#pragma unroll
+          for (int v = 0; v < 8; ++v) {
+            uint4 o;
+            __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              oh[u] = __floats2bfloat162_rn(acc[8 * v + 2 * u] * w, acc[8 * v + 2 * u + 1] * w);
+            dst[v] = o;
+          }
+        }
+      }
+    }
+    if (!ok) {
+      atomicOr(args.err, kErrTimeoutEpilogue);
+      *abort_flag = 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <bool kG1>
+cudaError_t launch_tm(const CUtensorMap& a, const CUtensorMap& b, const GemmArgs& args, int grid,
+                      cudaStream_t stream) {
+  using C = TmCfg<kG1>;
+  auto* fn = grouped_gemm_tm_kernel<kG1>;
+  static thread_local int configured_device = -1;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (configured_device != dev) {
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    configured_device = dev;
+  }
+  return launch_pdl(fn, dim3(grid), dim3(kTmThreads), C::kSmemBytes, stream, a, b, args);
+}
+
+}  // namespace
+
+cudaError_t launch_gemm1_tm(const CUtensorMap& a_map, const CUtensorMap& w13_map,
+                            const GemmArgs& args, int grid, cudaStream_t stream) {
+  return launch_tm<true>(a_map, w13_map, args, grid, stream);
+}
+
+cudaError_t launch_gemm2_tm(const CUtensorMap& cq_map, const CUtensorMap& w2_map,
+                            const GemmArgs& args, int grid, cudaStream_t stream) {
+  return launch_tm<false>(cq_map, w2_map, args, grid, stream);
+}
+
+}  // namespace fmoe

@@ -57,6 +57,19 @@ def test_validate_accepts_both_geometries(fmoe):
     assert lib.fmoe_validate(ctypes.byref(tiny)) == fmoe.FMOE_OK
 
 
+def test_validate_throughput_tile_needs_hidden_multiple_of_256(fmoe):
+    lib = fmoe.load_library()
+    p = _prob(fmoe, T=4096)
+    p.tile_n = 128
+    assert lib.fmoe_validate(ctypes.byref(p)) == fmoe.FMOE_OK
+    odd = fmoe.make_problem(64, 16, 16, 384, 128)
+    odd.tile_n = 128
+    assert lib.fmoe_validate(ctypes.byref(odd)) == fmoe.FMOE_ERR_VALUE
+    assert b"multiple of 256" in lib.fmoe_last_error()
+    odd.tile_n = 0  # the table's 128 falls back to the decode family instead
+    assert lib.fmoe_validate(ctypes.byref(odd)) == fmoe.FMOE_OK
+
+
 def test_workspace_size_grows_with_tokens(fmoe):
     sizes = [fmoe.workspace_bytes(_prob(fmoe, T=t)) for t in (1, 64, 4096)]
     assert sizes[0] < sizes[1] < sizes[2]

@@ -140,7 +140,7 @@ def test_forward_dsv3_decode(fmoe, oracle_mod, T):
     assert _device_error(fmoe, geo, T) == 0
 
 
-@pytest.mark.parametrize("tile_n", [16, 32, 64])
+@pytest.mark.parametrize("tile_n", [16, 32, 64, 128])
 def test_forward_dsv3_every_tile(fmoe, oracle_mod, tile_n):
     geo = W.DSV3
     T = 200
@@ -150,17 +150,31 @@ def test_forward_dsv3_every_tile(fmoe, oracle_mod, tile_n):
     assert _device_error(fmoe, geo, T, tile_n=tile_n) == 0
 
 
-@pytest.mark.parametrize("T,skew", [(512, 0), (4096, 0), (8192, 0), (4096, 8)],
-                         ids=["T512", "T4096", "T8192", "T4096_skew"])
-def test_forward_dsv3_large_sampled(fmoe, oracle_mod, T, skew):
+# tile 0 = the autotune table (decode family up to 2048 tokens, throughput family above);
+# the explicit tiles force the other family on the same inputs
+@pytest.mark.parametrize("T,skew,tile", [(512, 0, 0), (4096, 0, 0), (8192, 0, 0), (4096, 8, 0),
+                                         (4096, 0, 64), (4096, 8, 64), (1024, 0, 128)],
+                         ids=["T512", "T4096", "T8192", "T4096_skew", "T4096_tile64",
+                              "T4096_skew_tile64", "T1024_tile128"])
+def test_forward_dsv3_large_sampled(fmoe, oracle_mod, T, skew, tile):
     geo = W.DSV3
     gpu, cpu, cache = _inputs(geo, T, seed=2, skew_hot=skew)
-    out = _run(fmoe, geo, gpu, 0, 2.5)
+    out = _run(fmoe, geo, gpu, 0, 2.5, tile_n=tile)
     g = torch.Generator().manual_seed(T + skew)
     tokens = torch.randperm(T, generator=g)[:48].sort().values
     ref = _oracle(oracle_mod, geo, cpu, 0, 2.5, cache, tokens=tokens)
     _check(out[tokens.cuda()], ref)
-    assert _device_error(fmoe, geo, T) == 0
+    assert _device_error(fmoe, geo, T, tile_n=tile) == 0
+
+
+@pytest.mark.parametrize("T", [1, 16, 33, 100])
+@pytest.mark.parametrize("geo,offset", [(W.TINY, 0), (TINY_LOCAL, 8)], ids=["tiny", "tiny_slice8"])
+def test_forward_tiny_throughput_family(fmoe, oracle_mod, T, geo, offset):
+    """tile_n 128: 128 token rows per MMA tile, partly empty at these sizes."""
+    gpu, cpu, cache = _inputs(geo, T, seed=3)
+    out = _run(fmoe, geo, gpu, offset, 2.5, tile_n=128)
+    _check(out, _oracle(oracle_mod, geo, cpu, offset, 2.5, cache))
+    assert _device_error(fmoe, geo, T, offset, tile_n=128) == 0
 
 
 def test_plan_bitexact(fmoe, oracle_mod):
