@@ -6,7 +6,7 @@ metric quotes in "% HBM BW". One step = one call of the operator on one batch.
 A sweep over configs 1, 2 and 4 (T = 1..8192, skewed routing) is attached as "sweep".
 
   value      tokens/s with inputs resident in HBM, CUDA events around each call,
-             L2 flushed (256 MiB write) between timed calls
+             L2 flushed (256 MiB write, then read back) between timed calls
   e2e        tokens/s through the public API (fmoe_b200.kernel) with the activations
              copied from pinned host memory and the output copied back, every step
   roofline   GEMM1 (the dominant kernel): algorithmic bytes per launch / its average
@@ -146,6 +146,14 @@ def layer_bytes(T, active):
     return active * BYTES_PER_EXPERT + T * (7168 + 224 + 1024) + T * 7168 * 2
 
 
+def flush_l2(buf):
+    """Evict L2 between timed calls: write a buffer twice L2's size, then read it back, so
+    that the written lines are also written back to HBM here, outside the timed region (a
+    preceding layer leaves L2 holding other data, not 126 MB of dirty lines)."""
+    buf.zero_()
+    buf.sum()
+
+
 def time_device(inp, steps, warmup, flush, stage=False, tile_n=0):
     """Per-call device time (ms) with inputs resident; L2 flushed between calls."""
     args = W.operator_args(inp)
@@ -155,7 +163,7 @@ def time_device(inp, steps, warmup, flush, stage=False, tile_n=0):
     torch.cuda.synchronize()
     pairs, timers = [], []
     for _ in range(steps):
-        flush.zero_()
+        flush_l2(flush)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         if stage:
@@ -195,7 +203,7 @@ def time_graph(inp, steps, warmup, flush, tile_n=0):
     torch.cuda.synchronize()
     pairs = []
     for _ in range(steps):
-        flush.zero_()
+        flush_l2(flush)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -399,7 +407,7 @@ def run_reference(args, rank):
     torch.cuda.synchronize()
     pairs = []
     for _ in range(args.steps):
-        flush.zero_()
+        flush_l2(flush)
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record()
@@ -417,7 +425,7 @@ def run_reference(args, rank):
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, FP8 128-block scales)",
         "config": {"workload": f"config1_dsv3_decode_T{T}", "tokens": T, "hidden": 7168,
                    "intermediate": 2048, "experts": 256, "local_experts": 32, "top_k": 8,
-                   "l2": "flushed between calls (256 MiB write)"},
+                   "l2": "flushed between calls (256 MiB write, then read back)"},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": 1, "kind": "reference",
                          "sample": "reference solution/cuda/kernel.cu (its own CUDA code; it has "
@@ -537,7 +545,7 @@ def main():
                    "top_k": 8, "n_group": 8, "topk_group": 4, "routed_rows": rows,
                    "active_experts": active, "tile_n": fmoe_b200.load_library()
                    .fmoe_autotune_tile_n(T), "parallelism": f"replicas x{world}",
-                   "l2": "flushed between calls (256 MiB write); weights 1.2 GB > L2",
+                   "l2": "flushed between calls (256 MiB write, then read back); weights > L2",
                    "launch": "one CUDA graph replay per step (memset + 5 PDL kernels)"},
         "roofline": roofline, "clocks": clocks, "e2e": e2e,
         "gpu_launches": 5 * args.steps,

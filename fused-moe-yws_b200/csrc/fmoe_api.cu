@@ -119,22 +119,31 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// 2D byte tensor [outer, inner] with row pitch `pitch` bytes; box [box_outer, box_inner].
-int make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch,
-             uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz, const char* what) {
+// Byte tensor of rank 2 or 3: dims[0] is the contiguous one, strides[i] is the byte
+// distance between consecutive indices of dims[i + 1]; box[i] elements per dimension.
+int encode_map(CUtensorMap* map, const void* base, int rank, const cuuint64_t* dims,
+               const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle swz,
+               const char* what) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return fail(FMOE_ERR_RUNTIME, "cuTensorMapEncodeTiled unavailable");
-  const cuuint64_t dims[2] = {inner, outer};
-  const cuuint64_t strides[1] = {pitch};
-  const cuuint32_t box[2] = {box_inner, box_outer};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims,
-                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, (cuuint32_t)rank,
+                         const_cast<void*>(base), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return fail(FMOE_ERR_RUNTIME, std::string("tensor map encode failed for ") + what +
                                       " (CUresult " + std::to_string((int)r) + ")");
   return FMOE_OK;
+}
+
+// 2D byte tensor [outer, inner] with row pitch `pitch` bytes; box [box_outer, box_inner].
+int make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch,
+             uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz, const char* what) {
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {pitch};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  return encode_map(map, base, 2, dims, strides, box, swz, what);
 }
 
 int num_sms_current() {
@@ -311,20 +320,42 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   }
   if ((v = mark_stage(2, stream)) != FMOE_OK) return v;
 
+  // Tensor maps. Throughput family: token rows on the MMA M side (128-row boxes of tokens
+  // and of weights). Decode family: 32 KB of weights per box -- W13 as {K, row in half,
+  // (expert, gate|up)} with box {128, 128, 2}, W2 with 256-row boxes -- and the hi / lo
+  // token tiles of one C block as {byte in block, row, 128-byte block} with box {128, BN, 2}.
   CUtensorMap m_w13, m_a, m_w2, m_cq;
-  if ((v = make_map(&m_w13, t->gemm1_weights, H, (uint64_t)EL * 2 * I, H, 128, 128,
-                    CU_TENSOR_MAP_SWIZZLE_128B, "gemm1_weights")) != FMOE_OK)
-    return v;
+  uint8_t* cq = c.at<uint8_t>(c.L.cq);
   if ((v = make_map(&m_a, sa.a_perm, H, c.L.row_cap, H, 128, bn, CU_TENSOR_MAP_SWIZZLE_128B,
                     "permuted activations")) != FMOE_OK)
     return v;
-  if ((v = make_map(&m_w2, t->gemm2_weights, I, (uint64_t)EL * H, I, 128, 128,
-                    CU_TENSOR_MAP_SWIZZLE_128B, "gemm2_weights")) != FMOE_OK)
-    return v;
-  uint8_t* cq = c.at<uint8_t>(c.L.cq);
-  if ((v = make_map(&m_cq, cq, 2 * (uint64_t)I, c.L.row_cap, 2 * (uint64_t)I, 128, bn,
-                    CU_TENSOR_MAP_SWIZZLE_128B, "quantised intermediate")) != FMOE_OK)
-    return v;
+  if (tm) {
+    if ((v = make_map(&m_w13, t->gemm1_weights, H, (uint64_t)EL * 2 * I, H, 128, 128,
+                      CU_TENSOR_MAP_SWIZZLE_128B, "gemm1_weights")) != FMOE_OK)
+      return v;
+    if ((v = make_map(&m_w2, t->gemm2_weights, I, (uint64_t)EL * H, I, 128, 128,
+                      CU_TENSOR_MAP_SWIZZLE_128B, "gemm2_weights")) != FMOE_OK)
+      return v;
+    if ((v = make_map(&m_cq, cq, 2 * (uint64_t)I, c.L.row_cap, 2 * (uint64_t)I, 128, bn,
+                      CU_TENSOR_MAP_SWIZZLE_128B, "quantised intermediate")) != FMOE_OK)
+      return v;
+  } else {
+    const cuuint64_t d13[3] = {(cuuint64_t)H, (cuuint64_t)I, 2 * (cuuint64_t)EL};
+    const cuuint64_t s13[2] = {(cuuint64_t)H, (cuuint64_t)I * H};
+    const cuuint32_t b13[3] = {128, 128, 2};
+    if ((v = encode_map(&m_w13, t->gemm1_weights, 3, d13, s13, b13, CU_TENSOR_MAP_SWIZZLE_128B,
+                        "gemm1_weights")) != FMOE_OK)
+      return v;
+    if ((v = make_map(&m_w2, t->gemm2_weights, I, (uint64_t)EL * H, I, 128, 256,
+                      CU_TENSOR_MAP_SWIZZLE_128B, "gemm2_weights")) != FMOE_OK)
+      return v;
+    const cuuint64_t dq[3] = {128, (cuuint64_t)c.L.row_cap, 2 * (cuuint64_t)I / 128};
+    const cuuint64_t sq[2] = {2 * (cuuint64_t)I, 128};
+    const cuuint32_t bq[3] = {128, (cuuint32_t)bn, 2};
+    if ((v = encode_map(&m_cq, cq, 3, dq, sq, bq, CU_TENSOR_MAP_SWIZZLE_128B,
+                        "quantised intermediate")) != FMOE_OK)
+      return v;
+  }
 
   GemmArgs g;
   g.chunks = c.at<Chunk>(c.L.chunks);
@@ -353,7 +384,7 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
     FMOE_CUDA_TRY(launch_gemm1(bn, m_w13, m_a, g, grid1, stream));
   if ((v = mark_stage(3, stream)) != FMOE_OK) return v;
 
-  g.m_tiles = tm ? H / 256 : H / kBlock;
+  g.m_tiles = tm ? H / 256 : (H + 255) / 256;
   g.k_steps = I / kBlock;
   g.w_scale = t->gemm2_weights_scale;
   g.act_scale = g.c_scale;

@@ -17,16 +17,21 @@
 //   D * w_scale[row block, kb] * a_scale[token, kb] into fp32 registers. The tile
 //   epilogue forms C = x1 * silu(x2) and writes it as an FP8 hi/lo pair on one
 //   per-(token, 128-column) scale: C ~ scale * (hi + lo), relative error ~2^-8.
-// GEMM2: tile = 128 rows h of W2. Per 128-column C block j: D = W2[:, 128j:128j+128] .
-//   hi_j^T + W2[...] . lo_j^T (both into the same accumulator: same scale), promoted
-//   with w2_scale[h block, j] * c_scale[token, j]. Epilogue writes
-//   bf16(D * routing_weight) per routed row for the deterministic combine.
+// GEMM2: tile = 256 rows h of W2 (two 128-row accumulators). Per 128-column C block j, one
+//   MMA of N = 2 BN per accumulator over the stacked [hi_j; lo_j] token tiles gives
+//   W2[rows, 128j:128j+128] . hi_j^T and . lo_j^T side by side; their sum is promoted with
+//   w2_scale[h block, j] * c_scale[token, j]. The epilogue writes bf16(D * routing_weight)
+//   per routed row for the deterministic combine.
+// Each K step is three copies: one 32 KB weight box (GEMM1: gate and up tiles through a 3D
+// tensor map; GEMM2: a 256-row box), one token box (GEMM2: hi and lo through a 3D map) and
+// one bulk copy of the token scales -- the producer thread's issue cost is per copy.
 //
 // Warp roles (320 threads, one CTA per SM, persistent over the tile list):
 //   warp 0      TMA producer (one lane)
 //   warp 1      TMEM allocator + MMA issuer (one lane)
 //   warps 2..9  epilogue: warp w reads TMEM lane quadrant (w % 4), column half
-//               (w - 2) / 4 of the token tile.
+//               (w - 2) / 4 of the token tile; thread row r holds both accumulators'
+//               row r (GEMM1: gate and up of C column r; GEMM2: output rows r, 128 + r).
 // TMEM: 512 columns = two accumulator buffers of up to 256 columns, so the MMA of
 // K block kb+1 overlaps the promotion of block kb.
 #include <cuda_fp8.h>
@@ -49,16 +54,18 @@ constexpr int kBarAll = 3;          // named barrier id over all epilogue warps
 
 template <int BN, bool kG1>
 struct Cfg {
-  static constexpr int kAcc = kG1 ? 2 : 1;                    // accumulators per K step
-  static constexpr int kABytes = kG1 ? 2 * 128 * 128 : 128 * 128;  // gate+up or W2 rows
+  static constexpr int kAcc = 2;                              // accumulators per K step
+  static constexpr int kABytes = 2 * 128 * 128;               // gate + up, or 256 W2 rows
   static constexpr int kBBytes = (kG1 ? 1 : 2) * BN * 128;   // tokens (G2: hi and lo)
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int HB = BN / 2;                           // token columns per half
-  // TMEM load width; GEMM1 keeps two accumulators live, so it loads narrower chunks
-  static constexpr int kCWMax = kG1 ? 16 : 32;
+  // TMEM load width: two accumulators are live, so loads go in narrow chunks
+  static constexpr int kCWMax = 16;
   static constexpr int CW = HB < kCWMax ? HB : kCWMax;
-  static constexpr int kBNs = BN < 32 ? 32 : BN;              // TMEM column stride
-  static constexpr int kBufCols = kAcc * kBNs;
+  // TMEM columns per accumulator. GEMM2 runs one MMA of N = 2 BN over the stacked hi and
+  // lo token rows, so an accumulator holds W.hi in columns [0, BN) and W.lo in [BN, 2 BN)
+  static constexpr int kAccCols = kG1 ? (BN < 32 ? 32 : BN) : 2 * BN;
+  static constexpr int kBufCols = 2 * kAccCols;
   static constexpr int kNBufRaw = 512 / kBufCols;
   static constexpr int kNBuf = kNBufRaw > 8 ? 8 : kNBufRaw;   // accumulator ring depth
   static constexpr int kExBytes = kG1 ? 2 * 128 * (HB + 1) * 4 : 0;  // SwiGLU staging
@@ -104,6 +111,26 @@ __device__ __forceinline__ void promote(float (&acc)[HB], uint32_t taddr, const 
 #pragma unroll
       for (int i = 0; i < CW; ++i)
         acc[c * CW + i] = fmaf(__uint_as_float(v[i]), sa[c * CW + i] * sw, acc[c * CW + i]);
+    }
+  }
+}
+
+// GEMM2: acc[j] += (D_hi[row, col_j] + D_lo[row, col_j]) * scale_j * sw, the lo columns
+// `lo_off` TMEM columns after the hi columns.
+template <int HB, int CW>
+__device__ __forceinline__ void promote_hilo(float (&acc)[HB], uint32_t taddr, int lo_off,
+                                             const float* sa, float sw, int col0, int ncols) {
+#pragma unroll
+  for (int c = 0; c < HB / CW; ++c) {
+    if (col0 + c * CW < ncols) {
+      uint32_t h[CW], l[CW];
+      tmem_ld_32x32b<CW>(taddr + c * CW, h);
+      tmem_ld_32x32b<CW>(taddr + lo_off + c * CW, l);
+      tmem_ld_wait();
+#pragma unroll
+      for (int i = 0; i < CW; ++i)
+        acc[c * CW + i] = fmaf(__uint_as_float(h[i]) + __uint_as_float(l[i]),
+                               sa[c * CW + i] * sw, acc[c * CW + i]);
     }
   }
 }
@@ -266,13 +293,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           g = args.w_scale + ((int64_t)ch.expert * nb2 + m) * kbh;
           u = args.w_scale + ((int64_t)ch.expert * nb2 + args.I / kBlock + m) * kbh;
         } else {
-          g = args.w_scale + ((int64_t)ch.expert * (args.H / kBlock) + m) * kbh;
-          u = g;
+          // h blocks 2 m and 2 m + 1; the second is past the expert when H / 128 is odd
+          g = args.w_scale + ((int64_t)ch.expert * (args.H / kBlock) + 2 * m) * kbh;
+          u = 2 * m + 1 < args.H / kBlock ? g + kbh : nullptr;
         }
         float* dst = wsc + ws * 2 * kMaxKSteps;
         for (int i = lane; i < kbh; i += 32) {
           dst[i] = __ldg(g + i);
-          if constexpr (kG1) dst[kMaxKSteps + i] = __ldg(u + i);
+          dst[kMaxKSteps + i] = u ? __ldg(u + i) : 0.0f;
         }
         mbar_arrive(&wfull[ws]);  // every lane: its stores are released by its own arrive
         ++wseg;
@@ -290,15 +318,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sb = sa + C::kABytes;
           mbar_arrive_expect_tx(&full[s], C::kTx);
           if constexpr (kG1) {
-            const int wrow = ch.expert * 2 * args.I + m * 128;
-            tma_load_2d(sa, &tmA, &full[s], ks * 128, wrow, pol_w);
-            tma_load_2d(sa + 128 * 128, &tmA, &full[s], ks * 128, wrow + args.I, pol_w);
+            // {K, row in half, (expert, gate|up)} box {128, 128, 2}: gate tile, then up tile
+            tma_load_3d(sa, &tmA, &full[s], ks * 128, m * 128, 2 * ch.expert, pol_w);
             tma_load_2d(sb, &tmB, &full[s], ks * 128, ch.row0, pol_a);
           } else {
-            const int wrow = ch.expert * args.H + m * 128;
-            tma_load_2d(sa, &tmA, &full[s], ks * 128, wrow, pol_w);
-            tma_load_2d(sb, &tmB, &full[s], ks * 256, ch.row0, pol_a);             // hi
-            tma_load_2d(sb + BN * 128, &tmB, &full[s], ks * 256 + 128, ch.row0, pol_a);  // lo
+            // 256 W2 rows; {byte in block, row, 128-byte block} box {128, BN, 2}: hi, then lo
+            tma_load_2d(sa, &tmA, &full[s], ks * 128, ch.expert * args.H + m * 256, pol_w);
+            tma_load_3d(sb, &tmB, &full[s], 0, ch.row0, 2 * ks, pol_a);
           }
           // activation / intermediate scales of this K step for the chunk's columns
           mbar_arrive_expect_tx(&sfull[slot], ch.ncols * 4);
@@ -327,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int tile, k0, k1;
       while (ok && sched.next(tile, k0, k1)) {
         const Chunk ch = args.chunks[tile / args.m_tiles];
-        const uint32_t idesc = idesc_e4m3_f32(128, ch.ncols);
+        const uint32_t idesc = idesc_e4m3_f32(128, kG1 ? ch.ncols : 2 * BN);
         for (int ks = k0; ks < k1; ++ks, ++it) {
           const int b = it % NB, use = it / NB;
           if (!mbar_wait(&tempty[b], (use & 1) ^ 1, abort_flag)) {
@@ -342,24 +368,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           const uint32_t sa = smem_addr(stages + s * C::kStageBytes);
           const uint32_t d = tmem + b * C::kBufCols;
-          if constexpr (kG1) {
-            const uint64_t ag = smem_desc_kmajor(sa, 128);
-            const uint64_t au = smem_desc_kmajor(sa + 128 * 128, 128);
-            const uint64_t bd = smem_desc_kmajor(sa + C::kABytes, 128);
+          // accumulator 0: weight rows 0..127 of the stage, 1: rows 128..255. For GEMM2 the
+          // hi and lo token tiles are adjacent in shared memory, so one MMA of N = 2 BN
+          // multiplies a weight tile with both (an MMA costs about the same up to N = 64)
+          const uint64_t a0 = smem_desc_kmajor(sa, 128);
+          const uint64_t a1 = smem_desc_kmajor(sa + 128 * 128, 128);
+          const uint64_t bd = smem_desc_kmajor(sa + C::kABytes, 128);
 #pragma unroll
-            for (int sub = 0; sub < 4; ++sub) {
-              mma_f8f6f4(d, ag + 2 * sub, bd + 2 * sub, idesc, sub > 0);
-              mma_f8f6f4(d + C::kBNs, au + 2 * sub, bd + 2 * sub, idesc, sub > 0);
-            }
-          } else {
-            // hi and lo parts of the 128-column C block share one scale -> one accumulator
-            const uint64_t ad = smem_desc_kmajor(sa, 128);
-            const uint64_t bh = smem_desc_kmajor(sa + C::kABytes, 128);
-            const uint64_t bl = smem_desc_kmajor(sa + C::kABytes + BN * 128, 128);
-#pragma unroll
-            for (int sub = 0; sub < 4; ++sub) mma_f8f6f4(d, ad + 2 * sub, bh + 2 * sub, idesc, sub > 0);
-#pragma unroll
-            for (int sub = 0; sub < 4; ++sub) mma_f8f6f4(d, ad + 2 * sub, bl + 2 * sub, idesc, 1);
+          for (int sub = 0; sub < 4; ++sub) {
+            mma_f8f6f4(d, a0 + 2 * sub, bd + 2 * sub, idesc, sub > 0);
+            mma_f8f6f4(d + C::kAccCols, a1 + 2 * sub, bd + 2 * sub, idesc, sub > 0);
           }
           tc_commit(&empty[s]);
           tc_commit(&tfull[b]);
@@ -381,8 +399,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tid_e = ew * 32 + lane;  // 0..255
     const int r = q * 32 + lane;      // accumulator row = weight row inside the tile
     const int bar_half = 1 + half;    // named barrier of the 4 warps of this half
-    float acc_g[HB];
-    float acc_u[kG1 ? HB : 1];
+    float acc_g[HB];  // accumulator 0 (GEMM1 gate, GEMM2 rows 0..127 of the tile)
+    float acc_u[HB];  // accumulator 1 (GEMM1 up, GEMM2 rows 128..255)
     int it = 0, wseg = 0;
     bool ok = true;
     Schedule sched(num_tiles, KS, (int)gridDim.x, cta);
@@ -396,10 +414,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok && !mbar_wait(&wfull[ws], (wseg >> 1) & 1, abort_flag)) ok = false;
       const float* wrow = wsc + ws * 2 * kMaxKSteps;
 #pragma unroll
-      for (int j = 0; j < HB; ++j) acc_g[j] = 0.0f;
-      if constexpr (kG1) {
-#pragma unroll
-        for (int j = 0; j < HB; ++j) acc_u[j] = 0.0f;
+      for (int j = 0; j < HB; ++j) {
+        acc_g[j] = 0.0f;
+        acc_u[j] = 0.0f;
       }
       for (int ks = k0; ks < k1; ++ks, ++it) {
         const int b = it % NB, use = it / NB;
@@ -413,8 +430,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const float* sa = sring + slot * BN + half * HB;
         const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + b * C::kBufCols + half * HB;
-        promote<HB, CW>(acc_g, tb, sa, wrow[ks], half * HB, ncols);
-        if constexpr (kG1) promote<HB, CW>(acc_u, tb + C::kBNs, sa, wrow[kMaxKSteps + ks], half * HB, ncols);
+        if constexpr (kG1) {
+          promote<HB, CW>(acc_g, tb, sa, wrow[ks], half * HB, ncols);
+          promote<HB, CW>(acc_u, tb + C::kAccCols, sa, wrow[kMaxKSteps + ks], half * HB, ncols);
+        } else {
+          promote_hilo<HB, CW>(acc_g, tb, BN, sa, wrow[ks], half * HB, ncols);
+          promote_hilo<HB, CW>(acc_u, tb + C::kAccCols, BN, sa, wrow[kMaxKSteps + ks], half * HB,
+                               ncols);
+        }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
@@ -441,7 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int slot = sched.sk_begin() >= tile_begin ? 0 : 1;
         float* part = args.partials + (int64_t)(2 * cta + slot) * C::kPartialFloats;
         store_row<HB>(part + (0 * 128 + r) * BN + half * HB, acc_g);
-        if constexpr (kG1) store_row<HB>(part + (1 * 128 + r) * BN + half * HB, acc_u);
+        store_row<HB>(part + (1 * 128 + r) * BN + half * HB, acc_u);
         __threadfence();
         named_bar(kBarAll, kEpiThreads);
         const int cf = sk.cta_of(tile_begin), cl = sk.cta_of(tile_begin + KS - 1);
@@ -457,9 +480,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr int kRegs = 32;
         sum_contributions<HB, kRegs>(acc_g, args.partials, (0 * 128 + r) * BN + half * HB,
                                      C::kPartialFloats, sk, tile_begin, cf, cl);
-        if constexpr (kG1)
-          sum_contributions<HB, kRegs>(acc_u, args.partials, (1 * 128 + r) * BN + half * HB,
-                                       C::kPartialFloats, sk, tile_begin, cf, cl);
+        sum_contributions<HB, kRegs>(acc_u, args.partials, (1 * 128 + r) * BN + half * HB,
+                                     C::kPartialFloats, sk, tile_begin, cf, cl);
       }
 
       if constexpr (kG1) {
@@ -519,7 +541,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         named_bar(bar_half, 128);  // exh is reused by the next tile
       } else {
         // ---- weighted expert output rows, bf16, for the deterministic combine ----
-        const int h = m * 128 + r;
+        const int h = m * 256 + r;
+        const bool second = h + 128 < args.H;  // rows 128..255 exist unless H / 128 is odd
 #pragma unroll
         for (int j = 0; j < HB; ++j) {
           const int col = half * HB + j;
@@ -527,6 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int64_t row = ch.row0 + col;
             const float w = __ldg(args.row_w + row);
             args.ow[row * args.H + h] = __float2bfloat16_rn(acc_g[j] * w);
+            if (second) args.ow[row * args.H + h + 128] = __float2bfloat16_rn(acc_u[j] * w);
           }
         }
       }
@@ -564,6 +588,7 @@ cudaError_t launch_one(const CUtensorMap& a, const CUtensorMap& b, const GemmArg
 bool gemm_bn_supported(int bn) { return bn == 16 || bn == 32 || bn == 64 || bn == 128; }
 
 size_t gemm_partial_bytes() {
+  static_assert(Cfg<64, false>::kPartialFloats <= 128 * 256, "partial slot size");
   // stream-K: two partial slots per CTA; one partial tile is at most 2 accumulators x 128
   // rows x 64 columns of fp32 (decode GEMM1) or 128 token rows x 256 columns (throughput)
   return (size_t)2 * kMaxSms * 128 * 256 * sizeof(float);

@@ -32,60 +32,86 @@ __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
 }  // namespace
 
 __global__ void __launch_bounds__(256) scatter_gather_kernel(ScatterArgs a) {
-  __shared__ int s_le[kMaxEntries];
-  __shared__ int s_row[kMaxEntries];
-  __shared__ int s_list[kMaxEntries];
-  __shared__ int s_base[kMaxLocalExperts];
+  constexpr int kW = 8;  // warps
+  __shared__ int s_row[kMaxEntries];                 // destination row of each entry, or -1
+  __shared__ int s_list[kMaxEntries];                // entries with a local route, in order
+  __shared__ int s_base[kMaxLocalExperts];           // first row of each expert for this CTA
+  __shared__ int s_ecnt[kMaxLocalExperts];
+  __shared__ int s_eoff[kMaxLocalExperts];
+  __shared__ int s_wcnt[kW][kMaxLocalExperts];       // routes per (warp, expert) in a pass
+  __shared__ int s_wn[kW];
   __shared__ int s_nlocal;
 
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint32_t lt = (1u << lane) - 1u;
   const int K = a.top_k, nent = kTok * K;
   const int64_t t0 = (int64_t)blockIdx.x * kTok;
   pdl_wait();
   pdl_trigger();
-  for (int e = tid; e < a.E_local; e += blockDim.x)
-    s_base[e] = a.cta_base[(int64_t)blockIdx.x * a.E_local + e];
-  for (int i = tid; i < nent; i += blockDim.x) {
-    const int64_t t = t0 + i / K;
-    int le = -1;
-    if (t < a.T) {
-      const int ge = a.topk_idx[t * K + i % K];
-      const int l = ge - a.local_offset;
-      if (ge >= 0 && l >= 0 && l < a.E_local) le = l;
-    }
-    s_le[i] = le;
+  // every global index load of the CTA is issued in this one phase
+  for (int e = tid; e < a.E_local; e += blockDim.x) {
+    const int off = a.expert_off[e];
+    s_eoff[e] = off;
+    s_ecnt[e] = a.expert_cnt[e];
+    s_base[e] = off + a.cta_base[(int64_t)blockIdx.x * a.E_local + e];
   }
-  __syncthreads();
-  for (int i = tid; i < nent; i += blockDim.x) {
-    const int le = s_le[i];
-    const int64_t t = t0 + i / K;
+  if (tid == 0) s_nlocal = 0;
+  // stable rank of each entry (token-major, then k) among the CTA's entries of its expert:
+  // rank inside the warp from __match_any_sync, plus the earlier warps' counts
+  for (int p0 = 0; p0 < nent; p0 += blockDim.x) {
+    for (int i = tid; i < kW * a.E_local; i += blockDim.x) s_wcnt[i / a.E_local][i % a.E_local] = 0;
+    const int i = p0 + tid;
+    int le = -1;
+    if (i < nent) {
+      const int64_t t = t0 + i / K;
+      if (t < a.T) {
+        const int ge = a.topk_idx[t * K + i % K];
+        const int l = ge - a.local_offset;
+        if (ge >= 0 && l >= 0 && l < a.E_local) le = l;
+      }
+    }
+    const uint32_t peers = __match_any_sync(0xffffffffu, le);
+    __syncthreads();  // s_wcnt zeroed, s_base loaded
+    if (le >= 0 && (peers & lt) == 0u) s_wcnt[warp][le] = __popc(peers);
+    __syncthreads();
     int row = -1;
     if (le >= 0) {
-      int rank = 0;
-      for (int j = 0; j < i; ++j) rank += s_le[j] == le;
+      int rank = __popc(peers & lt);
+      for (int w = 0; w < warp; ++w) rank += s_wcnt[w][le];
       row = s_base[le] + rank;
       if (row >= a.row_cap) {
         atomicOr(a.meta + kMetaError, kErrRowOverflow);
         row = -1;
       }
     }
-    s_row[i] = row;
-    if (blockIdx.y == 0) {
+    // compact the local entries in entry order
+    const uint32_t has = __ballot_sync(0xffffffffu, row >= 0);
+    if (lane == 0) s_wn[warp] = __popc(has);
+    __syncthreads();
+    int pos = s_nlocal + __popc(has & lt);
+    for (int w = 0; w < warp; ++w) pos += s_wn[w];
+    if (i < nent) s_row[i] = row;
+    if (row >= 0) s_list[pos] = i;
+    if (blockIdx.y == 0 && i < nent) {
+      const int64_t t = t0 + i / K;
       if (t < a.T) a.token_row[t * K + i % K] = row;
       if (row >= 0) {
         a.row_token[row] = (int)t;
         a.row_w[row] = a.topk_w[t * K + i % K];
       }
     }
+    __syncthreads();  // all reads of s_nlocal / s_wn / s_wcnt of this pass are done
+    if (le >= 0) {
+      // later passes continue after this pass's rows of the same expert
+      if ((peers & lt) == 0u) atomicAdd(&s_base[le], __popc(peers));
+    }
+    if (tid == 0) {
+      int n = 0;
+      for (int w = 0; w < kW; ++w) n += s_wn[w];
+      s_nlocal += n;
+    }
+    __syncthreads();
   }
-  __syncthreads();
-  if (tid == 0) {
-    int n = 0;
-    for (int i = 0; i < nent; ++i)
-      if (s_row[i] >= 0) s_list[n++] = i;
-    s_nlocal = n;
-  }
-  __syncthreads();
   const int n = s_nlocal;
   // this CTA copies 16-byte column vectors [v0, v1) of every local row
   const int vpr = a.H / 16;
@@ -109,11 +135,12 @@ __global__ void __launch_bounds__(256) scatter_gather_kernel(ScatterArgs a) {
     }
   }
   // padding rows of the experts this CTA column owns (expert e goes to x = e % gridDim.x)
+  const uint4 z = make_uint4(0, 0, 0, 0);
   for (int e = blockIdx.x; e < a.E_local; e += gridDim.x) {
-    const int cnt = a.expert_cnt[e];
-    const int r0 = a.expert_off[e] + cnt;
+    const int cnt = s_ecnt[e];
+    const int r0 = s_eoff[e] + cnt;
     const int npad = (cnt + kRowAlign - 1) / kRowAlign * kRowAlign - cnt;
-    const uint4 z = make_uint4(0, 0, 0, 0);
+    if (npad == 0) continue;
     for (int v = tid; v < npad * vw; v += blockDim.x) {
       const int r = r0 + v / vw;
       if (r < a.row_cap)

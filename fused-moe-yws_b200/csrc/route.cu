@@ -53,6 +53,95 @@ __device__ __forceinline__ float key_value(uint32_t k) {
 }
 __device__ __forceinline__ bool is_candidate(float v) { return v > -INFINITY; }  // not NaN/-inf
 
+// Routing of one token when every group holds 32 experts (DeepSeek-V3: 8 groups of 32):
+// lane l owns expert g * 32 + l of every group g, so scores live in registers and every
+// selection step is a warp reduction. Same arithmetic, comparisons and summation order as
+// the general path below, hence the same bits.
+__device__ __forceinline__ void route_token_g32(const RouteArgs& a, int64_t t, int lane,
+                                                int* s_cnt) {
+  constexpr int kG = 8;  // groups per token supported here (E <= 256)
+  const int ng = a.n_group, K = a.top_k;
+  const float* lrow = a.logits + t * a.E;
+  float x[kG], b[kG], sg[kG], wb[kG];
+#pragma unroll
+  for (int g = 0; g < kG; ++g) {
+    x[g] = g < ng ? __ldg(lrow + g * 32 + lane) : 0.0f;
+    b[g] = g < ng ? bf16_bits_to_float(__ldg(a.bias + g * 32 + lane)) : 0.0f;
+  }
+#pragma unroll
+  for (int g = 0; g < kG; ++g) {
+    sg[g] = exact_sigmoid(x[g]);
+    wb[g] = g < ng ? __fadd_rn(sg[g], b[g]) : -INFINITY;
+  }
+  // group score = sum of the two largest candidates (duplicates count twice)
+  float gs[kG];
+#pragma unroll
+  for (int g = 0; g < kG; ++g) {
+    const uint32_t k = is_candidate(wb[g]) ? order_key(wb[g]) : 0u;
+    const uint32_t k1 = __reduce_max_sync(0xffffffffu, k);
+    const unsigned dup = __popc(__ballot_sync(0xffffffffu, k == k1 && k1 != 0u));
+    const uint32_t k2 = dup >= 2 ? k1 : __reduce_max_sync(0xffffffffu, k == k1 ? 0u : k);
+    gs[g] = __fadd_rn(k1 ? key_value(k1) : -INFINITY, k2 ? key_value(k2) : -INFINITY);
+  }
+  // kept groups: lane g (< n_group) counts the groups ranking above its own
+  const int mg = lane & (kG - 1);
+  float own = gs[0];
+#pragma unroll
+  for (int g = 1; g < kG; ++g)
+    if (g == mg) own = gs[g];
+  int rank = 0;
+#pragma unroll
+  for (int g = 0; g < kG; ++g)
+    if (g < ng && g != mg) rank += ranks_above(gs[g], g, own, mg);
+  const uint32_t keep =
+      __ballot_sync(0xffffffffu, lane < ng && rank < a.topk_group) & ((1u << ng) - 1u);
+  // top_k rounds: lane-local best (ties to the lower group = lower expert id), then the
+  // warp maximum, ties to the lowest expert id
+  uint32_t key[kG];
+#pragma unroll
+  for (int g = 0; g < kG; ++g)
+    key[g] = ((keep >> g) & 1u) && is_candidate(wb[g]) ? order_key(wb[g]) : 0u;
+  int my_e = -1;
+  float my_s = 0.0f, sum = 0.0f;
+  for (int k = 0; k < K; ++k) {
+    uint32_t bk = 0u;
+    int bg = 0;
+#pragma unroll
+    for (int g = 0; g < kG; ++g)
+      if (key[g] > bk) {
+        bk = key[g];
+        bg = g;
+      }
+    const uint32_t kmax = __reduce_max_sync(0xffffffffu, bk);
+    if (kmax == 0u) break;  // fewer than top_k candidates: the rest stay -1 / 0
+    const uint32_t win = __reduce_min_sync(
+        0xffffffffu, bk == kmax ? (uint32_t)(bg * 32 + lane) : 0xffffffffu);
+    const int wl = (int)(win & 31u), wg = (int)(win >> 5);
+    float v = sg[0];
+#pragma unroll
+    for (int g = 1; g < kG; ++g)
+      if (g == wg) v = sg[g];
+    v = __shfl_sync(0xffffffffu, v, wl);
+    sum = __fadd_rn(sum, v);  // selection order, as the reference sums
+    if (lane == wl) {
+#pragma unroll
+      for (int g = 0; g < kG; ++g)
+        if (g == wg) key[g] = 0u;
+    }
+    if (lane == k) {
+      my_e = (int)win;
+      my_s = v;
+    }
+  }
+  sum = __fadd_rn(sum, 1e-20f);
+  if (lane < K) {
+    a.topk_idx[t * K + lane] = my_e;
+    a.topk_w[t * K + lane] = my_e >= 0 ? __fmul_rn(__fdiv_rn(my_s, sum), a.rsf) : 0.0f;
+    const int le = my_e - a.local_offset;
+    if (my_e >= 0 && le >= 0 && le < a.E_local) atomicAdd(&s_cnt[le], 1);
+  }
+}
+
 __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
   __shared__ float s_sc[kWarps][kMaxE];
   __shared__ float s_wb[kWarps][kMaxE];
@@ -82,6 +171,8 @@ __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
       const int le = e - a.local_offset;
       if (e >= 0 && le >= 0 && le < a.E_local) atomicAdd(&s_cnt[le], 1);
     }
+  } else if (t < a.T && G == 32) {
+    route_token_g32(a, t, lane, s_cnt);
   } else if (t < a.T) {
     // 1) sigmoid + bias (strided, coalesced loads)
     const float* lrow = a.logits + t * E;
@@ -177,27 +268,44 @@ __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
     }
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < a.E_local; i += blockDim.x)
-    a.cta_counts[(int64_t)blockIdx.x * a.E_local + i] = s_cnt[i];
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int ticket = atomicAdd(a.meta + kMetaTicket, 1);
-    s_is_last = ticket == (int)gridDim.x - 1;
-  }
-  __syncthreads();
-  if (!s_is_last) return;
-  __threadfence();
-
-  // ---- last CTA: expert totals, 16-row aligned offsets, per-CTA bases, chunks ----
   const int nctas = gridDim.x;
-  const volatile int* cc = a.cta_counts;
+  if (nctas > 1) {
+    for (int i = threadIdx.x; i < a.E_local; i += blockDim.x)
+      a.cta_counts[(int64_t)blockIdx.x * a.E_local + i] = s_cnt[i];
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const int ticket = atomicAdd(a.meta + kMetaTicket, 1);
+      s_is_last = ticket == nctas - 1;
+    }
+    __syncthreads();
+    if (!s_is_last) return;
+    __threadfence();
+  }
+
+  // ---- last CTA: expert totals, per-CTA bases, 16-row aligned offsets, chunks ----
+  // cta_base[c][e] = rows of expert e routed by CTAs before c (relative to the expert's
+  // first row; the scatter adds expert_off[e])
   for (int e = warp; e < a.E_local; e += kWarps) {
-    int sum = 0;
-    for (int c = lane; c < nctas; c += 32) sum += cc[(int64_t)c * a.E_local + e];
+    int run = 0;
+    if (nctas == 1) {
+      run = s_cnt[e];
+      if (lane == 0) a.cta_base[e] = 0;
+    } else {
+      for (int c0 = 0; c0 < nctas; c0 += 32) {
+        const int c = c0 + lane;
+        const int v = c < nctas ? __ldcg(a.cta_counts + (int64_t)c * a.E_local + e) : 0;
+        int incl = v;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (lane == 0) s_tot[e] = sum;
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += y;
+        }
+        if (c < nctas) a.cta_base[(int64_t)c * a.E_local + e] = run + incl - v;
+        run += __shfl_sync(0xffffffffu, incl, 31);
+      }
+    }
+    if (lane == 0) s_tot[e] = run;
   }
   __syncthreads();
   if (warp == 0) {
@@ -249,22 +357,6 @@ __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
       ch.rows = n - r < a.bn ? n - r : a.bn;
       ch.ncols = (ch.rows + kRowAlign - 1) / kRowAlign * kRowAlign;
       a.chunks[s_choff[e] + c] = ch;
-    }
-  }
-  // per-CTA base row of each expert: expert offset + rows of the earlier CTAs
-  for (int e = warp; e < a.E_local; e += kWarps) {
-    int run = s_off[e];
-    for (int c0 = 0; c0 < nctas; c0 += 32) {
-      const int c = c0 + lane;
-      const int v = c < nctas ? cc[(int64_t)c * a.E_local + e] : 0;
-      int incl = v;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      if (c < nctas) a.cta_base[(int64_t)c * a.E_local + e] = run + incl - v;
-      run += __shfl_sync(0xffffffffu, incl, 31);
     }
   }
 }

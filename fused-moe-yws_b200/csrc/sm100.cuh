@@ -88,6 +88,18 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
+// 3D tiled load global -> shared (box laid out innermost dimension first), no multicast.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t x, int32_t y, int32_t z,
+                                            uint64_t cache_hint) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y), "r"(z),
+      "l"(cache_hint)
+      : "memory");
+}
+
 // 1D bulk copy global -> shared (16-byte aligned addresses, size a multiple of 16),
 // completion signalled on `bar` (complete_tx).
 __device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes,
