@@ -460,7 +460,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (k0 != 0 || k1 != KS) {
         // position of the tile in the stream-K step space
         const StreamK& sk = sched.sk;
-        const int64_t tile_begin = (int64_t)(tile - sched.dp_tiles) * KS;
+        const int64_t tile_begin = sched.tile_begin(tile);
         const int slot = sched.sk_begin() >= tile_begin ? 0 : 1;
         float* part = args.partials + (int64_t)(2 * cta + slot) * C::kPartialFloats;
         store_row<HB>(part + (0 * 128 + r) * BN + half * HB, acc_g);

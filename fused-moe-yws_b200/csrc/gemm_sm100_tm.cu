@@ -375,7 +375,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       // ---- stream-K partial tiles ([row][256] fp32), finished by the last contributor ----
       if (k0 != 0 || k1 != KS) {
         const StreamK& sk = sched.sk;
-        const int64_t tile_begin = (int64_t)(tile - sched.dp_tiles) * KS;
+        const int64_t tile_begin = sched.tile_begin(tile);
         const int slot = sched.sk_begin() >= tile_begin ? 0 : 1;
         float* part = args.partials + (int64_t)(2 * cta + slot) * C::kPartialFloats + row * 256;
         if constexpr (kG1) {
