@@ -15,8 +15,11 @@
 
 #include <climits>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "../../include/fmoe.h"
 #include "autotune_table.h"
@@ -410,16 +413,151 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
 }  // namespace
 }  // namespace fmoe
 
+namespace fmoe {
+namespace {
+
+// ---------------------------------------------------------------------- graph cache
+// A call whose arguments (problem, every pointer, workspace, device, stream) repeat is
+// replayed from a CUDA graph: the second identical call captures the operator (memset and
+// the five PDL-linked kernels) on a library-owned stream and every later one launches the
+// instantiated graph on the caller's stream, so the per-call cost is one graph launch
+// instead of six launches. The graph reads the buffers' current contents; only the
+// addresses and sizes are frozen, and they are the key. Calls whose stream is itself being
+// captured, calls with stage events on, and FMOE_GRAPH_CACHE=0 run eagerly.
+struct GraphKey {
+  fmoe_problem p;
+  fmoe_tensors t;
+  const void* in_idx;
+  const void* in_w;
+  void* ws;
+  size_t ws_bytes;
+  void* stream;
+  int device;
+};
+
+struct GraphEntry {
+  GraphKey key;
+  cudaGraphExec_t exec;  // null until the key has been seen twice
+  uint64_t last_use;
+};
+
+constexpr size_t kGraphCacheSize = 16;
+std::mutex g_graph_mu;
+std::vector<GraphEntry> g_graphs;
+uint64_t g_graph_clock = 0;
+
+bool graph_cache_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("FMOE_GRAPH_CACHE");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+bool same_key(const GraphKey& a, const GraphKey& b) {
+  return std::memcmp(&a, &b, sizeof(GraphKey)) == 0;
+}
+
+cudaStream_t capture_stream(int device) {
+  static std::mutex mu;
+  static std::vector<cudaStream_t> streams;
+  std::lock_guard<std::mutex> lock(mu);
+  if ((int)streams.size() <= device) streams.resize(device + 1, nullptr);
+  if (!streams[device]) {
+    cudaStream_t st = nullptr;
+    if (cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+    streams[device] = st;
+  }
+  return streams[device];
+}
+
+int forward_cached(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_idx,
+                   const float* in_w, void* workspace, size_t workspace_bytes,
+                   void* stream_ptr) {
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (!graph_cache_enabled() || g_stage_on || !p || !t || p->num_tokens <= 0 ||
+      cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone)
+    return run_forward(p, t, in_idx, in_w, workspace, workspace_bytes, stream_ptr);
+  GraphKey key;
+  std::memset(&key, 0, sizeof(key));  // padding bytes take part in the comparison
+  key.p = *p;
+  key.t = *t;
+  key.in_idx = in_idx;
+  key.in_w = in_w;
+  key.ws = workspace;
+  key.ws_bytes = workspace_bytes;
+  key.stream = stream_ptr;
+  FMOE_CUDA_TRY(cudaGetDevice(&key.device));
+
+  std::unique_lock<std::mutex> lock(g_graph_mu);
+  GraphEntry* hit = nullptr;
+  for (GraphEntry& e : g_graphs)
+    if (same_key(e.key, key)) hit = &e;
+  if (hit && hit->exec) {
+    hit->last_use = ++g_graph_clock;
+    cudaGraphExec_t exec = hit->exec;
+    lock.unlock();
+    FMOE_CUDA_TRY(cudaGraphLaunch(exec, stream));
+    return FMOE_OK;
+  }
+  if (!hit) {
+    // first sighting: remember the key (evicting the least recently used), run eagerly
+    if (g_graphs.size() >= kGraphCacheSize) {
+      size_t old = 0;
+      for (size_t i = 1; i < g_graphs.size(); ++i)
+        if (g_graphs[i].last_use < g_graphs[old].last_use) old = i;
+      if (g_graphs[old].exec) cudaGraphExecDestroy(g_graphs[old].exec);
+      g_graphs.erase(g_graphs.begin() + (std::ptrdiff_t)old);
+    }
+    g_graphs.push_back(GraphEntry{key, nullptr, ++g_graph_clock});
+    lock.unlock();
+    return run_forward(p, t, in_idx, in_w, workspace, workspace_bytes, stream_ptr);
+  }
+  // second sighting: capture on the library stream, then launch on the caller's stream
+  cudaStream_t cs = capture_stream(key.device);
+  if (!cs) {
+    lock.unlock();
+    return run_forward(p, t, in_idx, in_w, workspace, workspace_bytes, stream_ptr);
+  }
+  FMOE_CUDA_TRY(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+  const int v = run_forward(p, t, in_idx, in_w, workspace, workspace_bytes, cs);
+  cudaGraph_t graph = nullptr;
+  const cudaError_t ec = cudaStreamEndCapture(cs, &graph);
+  if (v != FMOE_OK) {
+    if (graph) cudaGraphDestroy(graph);
+    return v;
+  }
+  if (ec != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    return fail(FMOE_ERR_RUNTIME, std::string("graph capture failed: ") + cudaGetErrorString(ec));
+  }
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t ei = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ei != cudaSuccess)
+    return fail(FMOE_ERR_RUNTIME,
+                std::string("graph instantiation failed: ") + cudaGetErrorString(ei));
+  hit->exec = exec;
+  hit->last_use = ++g_graph_clock;
+  lock.unlock();
+  FMOE_CUDA_TRY(cudaGraphLaunch(exec, stream));
+  return FMOE_OK;
+}
+
+}  // namespace
+}  // namespace fmoe
+
 extern "C" int fmoe_forward(const fmoe_problem* p, const fmoe_tensors* t, void* workspace,
                             size_t workspace_bytes, void* stream_ptr) {
-  return run_forward(p, t, nullptr, nullptr, workspace, workspace_bytes, stream_ptr);
+  return forward_cached(p, t, nullptr, nullptr, workspace, workspace_bytes, stream_ptr);
 }
 
 extern "C" int fmoe_forward_routed(const fmoe_problem* p, const int32_t* topk_idx,
                                    const float* topk_w, const fmoe_tensors* t, void* workspace,
                                    size_t workspace_bytes, void* stream_ptr) {
   if (!topk_idx || !topk_w) return fail(FMOE_ERR_VALUE, "topk_idx / topk_w must not be NULL");
-  return run_forward(p, t, topk_idx, topk_w, workspace, workspace_bytes, stream_ptr);
+  return forward_cached(p, t, topk_idx, topk_w, workspace, workspace_bytes, stream_ptr);
 }
 
 extern "C" int fmoe_set_stage_events(void* const* events) {
