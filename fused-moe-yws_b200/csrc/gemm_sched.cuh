@@ -65,10 +65,45 @@ struct Schedule {
     return false;
   }
   __device__ __forceinline__ int64_t sk_begin() const { return sk.start(cta); }
+  // Every CTA's stream-K range spans at least KS steps, so a split tile shared by two CTAs
+  // has its tail done as the second CTA's first split segment, long before the first CTA
+  // reaches the tile's head as its last segment.
+  __device__ __forceinline__ bool ranges_cover_a_tile() const { return sk.W / G >= KS; }
   // first global stream-K step of a split tile
   __device__ __forceinline__ int64_t tile_begin(int tile) const {
     return (int64_t)(tile - dp_tiles) * KS;
   }
 };
+
+// How a segment takes part in the fix-up of a split tile. Contributors are the CTAs
+// cf .. cl holding the tile's K steps in order.
+//   pair: exactly two contributors and ranges_cover_a_tile(): the head owner cf finishes
+//     the tile. The tail owner cl stores its fp32 partial (slot 0) and release-adds its
+//     step count to counter[cf], without waiting; cf, at the start of its head segment,
+//     waits for that count, loads the partial as its accumulator's starting value,
+//     accumulates its own steps on top and finalizes -- no fix-up at the end of the run.
+//   otherwise every contributor stores a partial and adds to counter[cf]; the one whose
+//     add completes the K range sums all partials in K order and finalizes.
+struct SplitRole {
+  bool split;     // the segment does not cover the whole tile
+  bool pair;      // two-contributor protocol
+  bool head;      // this CTA holds the tile's first K step
+  int cf, cl;     // contributor CTAs
+  int slot;       // partial slot of this CTA for the tile
+  int64_t tb;     // first stream-K step of the tile
+};
+
+__device__ __forceinline__ SplitRole split_role(const Schedule& sc, int tile, int k0, int k1) {
+  SplitRole r{};
+  r.split = k0 != 0 || k1 != sc.KS;
+  if (!r.split) return r;
+  r.tb = sc.tile_begin(tile);
+  r.cf = sc.sk.cta_of(r.tb);
+  r.cl = sc.sk.cta_of(r.tb + sc.KS - 1);
+  r.slot = sc.sk_begin() >= r.tb ? 0 : 1;
+  r.pair = r.cl == r.cf + 1 && sc.ranges_cover_a_tile();
+  r.head = k0 == 0;
+  return r;
+}
 
 }  // namespace fmoe

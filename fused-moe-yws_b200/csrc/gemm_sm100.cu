@@ -148,6 +148,24 @@ __device__ __forceinline__ void store_row(float* dst, const float (&v)[HB]) {
   }
 }
 
+// Load HB floats (16-byte aligned) written by another CTA: L2-coherent loads.
+template <int HB>
+__device__ __forceinline__ void load_row(float (&v)[HB], const float* src) {
+  if constexpr (HB % 4 == 0) {
+#pragma unroll
+    for (int j = 0; j < HB; j += 4) {
+      const float4 x = __ldcg(reinterpret_cast<const float4*>(src + j));
+      v[j] = x.x;
+      v[j + 1] = x.y;
+      v[j + 2] = x.z;
+      v[j + 3] = x.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < HB; ++j) v[j] = __ldcg(src + j);
+  }
+}
+
 // acc = sum of the tile's contributions in K order (contributor CTAs cf..cl, each of
 // which -- this one included -- has stored its partial before the arrival counter).
 // A contributor's partial lives in slot 0 (its range starts inside the tile) or slot 1
@@ -418,6 +436,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         acc_g[j] = 0.0f;
         acc_u[j] = 0.0f;
       }
+      const SplitRole role = split_role(sched, tile, k0, k1);
+      if (role.split && role.pair && role.head) {
+        // the tile's tail was this CTA's successor's first split segment: wait for its
+        // partial and start the accumulators from it (overlaps the first K steps' MMAs)
+        bool ready = true;
+        if (tid_e == 0 && ok) ready = wait_nonzero(args.tile_counters + role.cf, abort_flag);
+        if (named_bar_or(kBarAll, kEpiThreads, !ready || !ok)) {
+          if (ok) set_error(args.err, abort_flag, kErrTimeoutEpilogue);
+          ok = false;
+        } else {
+          const float* pp = args.partials + (int64_t)(2 * role.cl) * C::kPartialFloats;
+          load_row<HB>(acc_g, pp + (0 * 128 + r) * BN + half * HB);
+          load_row<HB>(acc_u, pp + (1 * 128 + r) * BN + half * HB);
+        }
+      }
       for (int ks = k0; ks < k1; ++ks, ++it) {
         const int b = it % NB, use = it / NB;
         const int slot = it % SR, suse = it / SR;
@@ -457,11 +490,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 
       // ---- stream-K: a partial segment publishes its fp32 partial; the contributor that
       //      completes the tile's K range sums all contributions in K order and finishes ----
-      if (k0 != 0 || k1 != KS) {
+      if (role.split && role.pair) {
+        float* part = args.partials + (int64_t)(2 * cta + role.slot) * C::kPartialFloats;
+        if (!role.head) {
+          // tail owner: publish the partial and move on (the head owner finishes the tile)
+          store_row<HB>(part + (0 * 128 + r) * BN + half * HB, acc_g);
+          store_row<HB>(part + (1 * 128 + r) * BN + half * HB, acc_u);
+          named_bar(kBarAll, kEpiThreads);
+          if (tid_e == 0) red_release_add(args.tile_counters + role.cf, k1 - k0);
+          continue;
+        }
+        if (tid_e == 0) args.tile_counters[role.cf] = 0;  // ready for the next launch
+      } else if (role.split) {
         // position of the tile in the stream-K step space
         const StreamK& sk = sched.sk;
-        const int64_t tile_begin = sched.tile_begin(tile);
-        const int slot = sched.sk_begin() >= tile_begin ? 0 : 1;
+        const int64_t tile_begin = role.tb;
+        const int slot = role.slot;
         float* part = args.partials + (int64_t)(2 * cta + slot) * C::kPartialFloats;
         store_row<HB>(part + (0 * 128 + r) * BN + half * HB, acc_g);
         store_row<HB>(part + (1 * 128 + r) * BN + half * HB, acc_u);

@@ -81,6 +81,19 @@ __device__ __forceinline__ void store_vec(float* dst, const float (&v)[N]) {
     *reinterpret_cast<float4*>(dst + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
 }
 
+// Load N floats written by another CTA (16-byte aligned): L2-coherent loads.
+template <int N>
+__device__ __forceinline__ void load_vec(float (&v)[N], const float* src) {
+#pragma unroll
+  for (int j = 0; j < N; j += 4) {
+    const float4 x = __ldcg(reinterpret_cast<const float4*>(src + j));
+    v[j] = x.x;
+    v[j + 1] = x.y;
+    v[j + 2] = x.z;
+    v[j + 3] = x.w;
+  }
+}
+
 // Sum of a tile's stream-K contributions (partials in [row][256] layout), in K order; CTAs
 // with an empty range contribute nothing. Partials come from other CTAs: L2-coherent loads.
 template <int N>
@@ -338,6 +351,27 @@ __global__ void __launch_bounds__(kTmThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) acc_u[i] = 0.0f;
       }
+      const SplitRole role = split_role(sched, tile, k0, k1);
+      if (role.split && role.pair && role.head) {
+        // start from the tail owner's partial (see SplitRole)
+        bool ready = true;
+        if (tid_e == 0 && ok) ready = wait_nonzero(args.tile_counters + role.cf, abort_flag);
+        if (named_bar_or(kTmBarAll, kTmEpiThreads, !ready || !ok)) {
+          if (ok) {
+            atomicOr(args.err, kErrTimeoutEpilogue);
+            *abort_flag = 1;
+          }
+          ok = false;
+        } else {
+          const float* pp = args.partials + (int64_t)(2 * role.cl) * C::kPartialFloats + row * 256;
+          if constexpr (kG1) {
+            load_vec<32>(acc, pp + 32 * j);
+            load_vec<32>(acc_u, pp + 128 + 32 * j);
+          } else {
+            load_vec<64>(acc, pp + 64 * j);
+          }
+        }
+      }
       for (int ks = k0; ks < k1; ++ks, ++it) {
         const int b = it % NB, use = it / NB;
         const int slot = it % SR, suse = it / SR;
@@ -373,10 +407,26 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         break;
       }
       // ---- stream-K partial tiles ([row][256] fp32), finished by the last contributor ----
-      if (k0 != 0 || k1 != KS) {
+      if (role.split && role.pair) {
+        if (!role.head) {
+          // tail owner: publish the partial and move on (the head owner finishes the tile)
+          float* part =
+              args.partials + (int64_t)(2 * cta + role.slot) * C::kPartialFloats + row * 256;
+          if constexpr (kG1) {
+            store_vec<32>(part + 32 * j, acc);
+            store_vec<32>(part + 128 + 32 * j, acc_u);
+          } else {
+            store_vec<64>(part + 64 * j, acc);
+          }
+          named_bar(kTmBarAll, kTmEpiThreads);
+          if (tid_e == 0) red_release_add(args.tile_counters + role.cf, k1 - k0);
+          continue;
+        }
+        if (tid_e == 0) args.tile_counters[role.cf] = 0;  // ready for the next launch
+      } else if (role.split) {
         const StreamK& sk = sched.sk;
-        const int64_t tile_begin = sched.tile_begin(tile);
-        const int slot = sched.sk_begin() >= tile_begin ? 0 : 1;
+        const int64_t tile_begin = role.tb;
+        const int slot = role.slot;
         float* part = args.partials + (int64_t)(2 * cta + slot) * C::kPartialFloats + row * 256;
         if constexpr (kG1) {
           store_vec<32>(part + 32 * j, acc);

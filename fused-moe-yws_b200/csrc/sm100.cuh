@@ -246,5 +246,30 @@ __device__ __forceinline__ void named_bar(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
+// ----------------------------------------------------------------------------- flags
+// Release add on a global counter, no return value: writes the issuing CTA made before
+// (ordered by a preceding barrier) are visible GPU-wide before the add is.
+__device__ __forceinline__ void red_release_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Wait until *p != 0 (acquire). Bounded like mbar_wait: false on timeout or abort.
+__device__ __forceinline__ bool wait_nonzero(const int* p, const volatile int* abort) {
+  if (ld_acquire(p) != 0) return true;
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+    __nanosleep(128);
+    if (ld_acquire(p) != 0) return true;
+    if (*abort) return false;
+    if (globaltimer() - t0 > kWaitTimeoutNs) return false;
+  }
+}
+
 }  // namespace sm100
 }  // namespace fmoe

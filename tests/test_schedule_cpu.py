@@ -57,11 +57,15 @@ class Schedule:
     def tile_begin(self, tile):
         return (tile - self.dp_tiles) * self.KS
 
+    def ranges_cover_a_tile(self):
+        return self.sk.W // self.G >= self.KS
+
 
 def simulate(num_tiles, ks, grid):
     cover = {}
     counters = {}
     partial_slots = {}
+    pairs = set()
     for c in range(grid):
         s = Schedule(num_tiles, ks, grid, c)
         seen_split = False
@@ -85,6 +89,18 @@ def simulate(num_tiles, ks, grid):
                 readers = [x for x in range(cf, cl + 1) if s.sk.start(x) != s.sk.start(x + 1)]
                 for x in readers:
                     assert s.sk.start(x) < tb + ks and s.sk.start(x + 1) > tb
+                if cl == cf + 1 and s.ranges_cover_a_tile():
+                    # two-contributor protocol: the tail is the tail owner's first split
+                    # segment, stored in slot 0; the head is the head owner's last segment;
+                    # counting steps at equal speed, the tail is done before the head starts
+                    tail_owner = Schedule(num_tiles, ks, grid, cl)
+                    head_owner = Schedule(num_tiles, ks, grid, cf)
+                    head_len = tb + ks - tb - (tb + ks - s.sk.start(cl))
+                    tail_len = ks - head_len
+                    assert tail_owner.sk_begin() >= tb  # slot 0
+                    assert head_owner.sk.start(cf + 1) == tb + head_len  # head ends cf's range
+                    assert tail_len <= (head_owner.sk.start(cf + 1) - head_owner.sk_begin()) - head_len
+                    pairs.add(tile)
             elif not s.is_split_tile(tile):
                 assert not seen_split, "whole tile after a split segment"
     for t in range(num_tiles):
