@@ -142,8 +142,10 @@ __device__ __forceinline__ float exact_expf(float x) {
   return __fmul_rn(__fmul_rn(p, pow2i_dev(n1)), pow2i_dev(n2));
 }
 
+// 1 / (1 + e) correctly rounded: __frcp_rn(d) is the IEEE quotient 1 / d, so it equals
+// the host's 1.0f / d bit for bit.
 __device__ __forceinline__ float exact_sigmoid(float x) {
-  return __fdiv_rn(1.0f, __fadd_rn(1.0f, exact_expf(-x)));
+  return __frcp_rn(__fadd_rn(1.0f, exact_expf(-x)));
 }
 
 }  // namespace fmoe

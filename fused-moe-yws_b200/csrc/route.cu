@@ -30,10 +30,9 @@ constexpr int kMaxGroups = 32;
 // True when (va, ia) ranks above (vb, ib): larger value, then smaller index; NaN lowest.
 __device__ __forceinline__ bool ranks_above(float va, int ia, float vb, int ib) {
   const bool na = va != va, nb = vb != vb;
-  if (na || nb) return (na && nb) ? ia < ib : nb;
-  if (va > vb) return true;
-  if (va < vb) return false;
-  return ia < ib;
+  const bool by_nan = (na && nb) ? ia < ib : nb;
+  const bool by_value = va > vb || (va == vb && ia < ib);
+  return (na || nb) ? by_nan : by_value;
 }
 
 __device__ __forceinline__ float bf16_bits_to_float(uint16_t b) {
@@ -53,83 +52,132 @@ __device__ __forceinline__ float key_value(uint32_t k) {
 }
 __device__ __forceinline__ bool is_candidate(float v) { return v > -INFINITY; }  // not NaN/-inf
 
-// Routing of one token when every group holds 32 experts (DeepSeek-V3: 8 groups of 32):
-// lane l owns expert g * 32 + l of every group g, so scores live in registers and every
-// selection step is a warp reduction. Same arithmetic, comparisons and summation order as
-// the general path below, hence the same bits.
+// (key, index) a ranks before (key, index) b: larger key, then smaller index.
+__device__ __forceinline__ bool before(uint32_t ka, int ia, uint32_t kb, int ib) {
+  return ka > kb || (ka == kb && ia < ib);
+}
+
+__device__ __forceinline__ void cswap(uint32_t (&k)[8], int (&ix)[8], int i, int j) {
+  if (!before(k[i], ix[i], k[j], ix[j])) {
+    const uint32_t tk = k[i];
+    k[i] = k[j];
+    k[j] = tk;
+    const int ti = ix[i];
+    ix[i] = ix[j];
+    ix[j] = ti;
+  }
+}
+
+// Batcher's odd-even merge sort of 8 (19 comparators), descending by (key, -index).
+__device__ __forceinline__ void sort8(uint32_t (&k)[8], int (&ix)[8]) {
+  cswap(k, ix, 0, 1); cswap(k, ix, 2, 3); cswap(k, ix, 4, 5); cswap(k, ix, 6, 7);
+  cswap(k, ix, 0, 2); cswap(k, ix, 1, 3); cswap(k, ix, 4, 6); cswap(k, ix, 5, 7);
+  cswap(k, ix, 1, 2); cswap(k, ix, 5, 6);
+  cswap(k, ix, 0, 4); cswap(k, ix, 1, 5); cswap(k, ix, 2, 6); cswap(k, ix, 3, 7);
+  cswap(k, ix, 2, 4); cswap(k, ix, 3, 5);
+  cswap(k, ix, 1, 2); cswap(k, ix, 3, 4); cswap(k, ix, 5, 6);
+}
+
+// Routing of one token when every group holds 32 experts (DeepSeek-V3: 8 groups of 32).
+// Lane l owns the 8 consecutive experts g * 32 + (l & 3) * 8 + i of group g = l >> 2, so
+// the group's top-2 is an in-lane top-2 merged over its 4 lanes by two shuffles, the kept
+// groups are ranked from 8 shuffled scores, and each top_k round takes the best head of
+// the lanes' sorted candidate lists (one redux; a second one only on an exact tie). Same
+// arithmetic, comparisons and summation order as the general path below, hence the same
+// bits; a single warp's dependency chain is the cost, so it is kept short.
 __device__ __forceinline__ void route_token_g32(const RouteArgs& a, int64_t t, int lane,
                                                 int* s_cnt) {
-  constexpr int kG = 8;  // groups per token supported here (E <= 256)
   const int ng = a.n_group, K = a.top_k;
-  const float* lrow = a.logits + t * a.E;
-  float x[kG], b[kG], sg[kG], wb[kG];
+  const int g = lane >> 2;
+  const bool live = g < ng;
+  const int e0 = g * 32 + (lane & 3) * 8;
+  float sg[8];
+  uint32_t key[8];
+  if (live) {
+    const float4* lp = reinterpret_cast<const float4*>(a.logits + t * a.E + e0);
+    const float4 x0 = __ldg(lp), x1 = __ldg(lp + 1);
+    const uint4 bv = __ldg(reinterpret_cast<const uint4*>(a.bias + e0));
+    const float x[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+    const uint32_t bw[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
-  for (int g = 0; g < kG; ++g) {
-    x[g] = g < ng ? __ldg(lrow + g * 32 + lane) : 0.0f;
-    b[g] = g < ng ? bf16_bits_to_float(__ldg(a.bias + g * 32 + lane)) : 0.0f;
+    for (int i = 0; i < 8; ++i) {
+      sg[i] = exact_sigmoid(x[i]);
+      const uint16_t bbits = (uint16_t)(bw[i >> 1] >> ((i & 1) * 16));
+      const float wb = __fadd_rn(sg[i], bf16_bits_to_float(bbits));
+      key[i] = is_candidate(wb) ? order_key(wb) : 0u;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      sg[i] = 0.0f;
+      key[i] = 0u;
+    }
+  }
+  // group score = sum of the two largest candidates (duplicates count twice): in-lane
+  // top-2, then merged across the group's 4 lanes
+  uint32_t m1 = 0u, m2 = 0u;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    m2 = max(m2, min(m1, key[i]));
+    m1 = max(m1, key[i]);
   }
 #pragma unroll
-  for (int g = 0; g < kG; ++g) {
-    sg[g] = exact_sigmoid(x[g]);
-    wb[g] = g < ng ? __fadd_rn(sg[g], b[g]) : -INFINITY;
+  for (int o = 1; o <= 2; o <<= 1) {
+    const uint32_t p1 = __shfl_xor_sync(0xffffffffu, m1, o);
+    const uint32_t p2 = __shfl_xor_sync(0xffffffffu, m2, o);
+    m2 = max(min(m1, p1), max(m2, p2));
+    m1 = max(m1, p1);
   }
-  // group score = sum of the two largest candidates (duplicates count twice)
-  float gs[kG];
-#pragma unroll
-  for (int g = 0; g < kG; ++g) {
-    const uint32_t k = is_candidate(wb[g]) ? order_key(wb[g]) : 0u;
-    const uint32_t k1 = __reduce_max_sync(0xffffffffu, k);
-    const unsigned dup = __popc(__ballot_sync(0xffffffffu, k == k1 && k1 != 0u));
-    const uint32_t k2 = dup >= 2 ? k1 : __reduce_max_sync(0xffffffffu, k == k1 ? 0u : k);
-    gs[g] = __fadd_rn(k1 ? key_value(k1) : -INFINITY, k2 ? key_value(k2) : -INFINITY);
-  }
-  // kept groups: lane g (< n_group) counts the groups ranking above its own
-  const int mg = lane & (kG - 1);
-  float own = gs[0];
-#pragma unroll
-  for (int g = 1; g < kG; ++g)
-    if (g == mg) own = gs[g];
+  const float gs =
+      __fadd_rn(m1 ? key_value(m1) : -INFINITY, m2 ? key_value(m2) : -INFINITY);
+  // kept groups: each lane counts the groups ranking above its own group
   int rank = 0;
 #pragma unroll
-  for (int g = 0; g < kG; ++g)
-    if (g < ng && g != mg) rank += ranks_above(gs[g], g, own, mg);
-  const uint32_t keep =
-      __ballot_sync(0xffffffffu, lane < ng && rank < a.topk_group) & ((1u << ng) - 1u);
-  // top_k rounds: lane-local best (ties to the lower group = lower expert id), then the
-  // warp maximum, ties to the lowest expert id
-  uint32_t key[kG];
+  for (int h = 0; h < 8; ++h) {
+    const float gh = __shfl_sync(0xffffffffu, gs, 4 * h);
+    if (h < ng && h != g) rank += ranks_above(gh, h, gs, g);
+  }
+  const bool keep = live && rank < a.topk_group;
+  // this lane's candidates, sorted (ties: lower expert id first)
+  int ix[8];
 #pragma unroll
-  for (int g = 0; g < kG; ++g)
-    key[g] = ((keep >> g) & 1u) && is_candidate(wb[g]) ? order_key(wb[g]) : 0u;
+  for (int i = 0; i < 8; ++i) {
+    ix[i] = i;
+    if (!keep) key[i] = 0u;
+  }
+  sort8(key, ix);
   int my_e = -1;
   float my_s = 0.0f, sum = 0.0f;
+  int head = 0;  // next unselected entry of the sorted list
   for (int k = 0; k < K; ++k) {
-    uint32_t bk = 0u;
-    int bg = 0;
+    uint32_t hk = 0u;
+    int hi = 0;
 #pragma unroll
-    for (int g = 0; g < kG; ++g)
-      if (key[g] > bk) {
-        bk = key[g];
-        bg = g;
+    for (int j = 0; j < 8; ++j)
+      if (j == head) {
+        hk = key[j];
+        hi = ix[j];
       }
-    const uint32_t kmax = __reduce_max_sync(0xffffffffu, bk);
+    const uint32_t kmax = __reduce_max_sync(0xffffffffu, hk);
     if (kmax == 0u) break;  // fewer than top_k candidates: the rest stay -1 / 0
-    const uint32_t win = __reduce_min_sync(
-        0xffffffffu, bk == kmax ? (uint32_t)(bg * 32 + lane) : 0xffffffffu);
-    const int wl = (int)(win & 31u), wg = (int)(win >> 5);
+    const unsigned tie = __ballot_sync(0xffffffffu, hk == kmax);
+    int win;
+    if ((tie & (tie - 1u)) == 0u) {
+      win = __shfl_sync(0xffffffffu, e0 + hi, __ffs(tie) - 1);
+    } else {
+      win = (int)__reduce_min_sync(0xffffffffu,
+                                   hk == kmax ? (uint32_t)(e0 + hi) : 0xffffffffu);
+    }
+    const int wl = win >> 3;  // the lane holding expert `win`
     float v = sg[0];
 #pragma unroll
-    for (int g = 1; g < kG; ++g)
-      if (g == wg) v = sg[g];
+    for (int j = 1; j < 8; ++j)
+      if (j == hi) v = sg[j];
     v = __shfl_sync(0xffffffffu, v, wl);
     sum = __fadd_rn(sum, v);  // selection order, as the reference sums
-    if (lane == wl) {
-#pragma unroll
-      for (int g = 0; g < kG; ++g)
-        if (g == wg) key[g] = 0u;
-    }
+    if (lane == wl) ++head;
     if (lane == k) {
-      my_e = (int)win;
+      my_e = win;
       my_s = v;
     }
   }
