@@ -59,7 +59,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 // Wait for the phase with the given parity to complete. Returns false on timeout or
 // when *abort becomes non-zero (another role gave up), never spins forever.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
-                                          const volatile int* abort) {
+                                          const volatile int* abort,
+                                          uint64_t timeout_ns = kWaitTimeoutNs) {
   const uint32_t a = smem_addr(bar);
   if (mbar_try_wait(a, parity)) return true;
   uint64_t t0 = globaltimer();
@@ -67,7 +68,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
     if (mbar_try_wait(a, parity)) return true;
     if ((i & 63) == 0) {
       if (*abort) return false;
-      if (globaltimer() - t0 > kWaitTimeoutNs) return false;
+      if (globaltimer() - t0 > timeout_ns) return false;
     }
   }
 }
@@ -260,14 +261,15 @@ __device__ __forceinline__ int ld_acquire(const int* p) {
 }
 
 // Wait until *p != 0 (acquire). Bounded like mbar_wait: false on timeout or abort.
-__device__ __forceinline__ bool wait_nonzero(const int* p, const volatile int* abort) {
+__device__ __forceinline__ bool wait_nonzero(const int* p, const volatile int* abort,
+                                             uint64_t timeout_ns = kWaitTimeoutNs) {
   if (ld_acquire(p) != 0) return true;
   const uint64_t t0 = globaltimer();
   for (;;) {
     __nanosleep(128);
     if (ld_acquire(p) != 0) return true;
     if (*abort) return false;
-    if (globaltimer() - t0 > kWaitTimeoutNs) return false;
+    if (globaltimer() - t0 > timeout_ns) return false;
   }
 }
 

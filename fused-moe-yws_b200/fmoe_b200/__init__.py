@@ -32,7 +32,7 @@ FMOE_OK, FMOE_ERR_VALUE, FMOE_ERR_TYPE, FMOE_ERR_RUNTIME, FMOE_ERR_WORKSPACE, FM
 EXPORTED_SYMBOLS = ("fmoe_abi_version", "fmoe_last_error", "fmoe_validate", "fmoe_workspace_size",
                     "fmoe_autotune_tile_n", "fmoe_forward", "fmoe_route", "fmoe_read_device_error",
                     "fmoe_plan_view_get", "fmoe_set_stage_events", "fmoe_route_static",
-                    "fmoe_forward_routed")
+                    "fmoe_forward_routed", "fmoe_selftest_wait_timeout")
 
 
 class FmoeProblem(ctypes.Structure):
@@ -91,6 +91,9 @@ def load_library(path: Path | str | None = None):
         lib.fmoe_plan_view_get.argtypes = [ctypes.POINTER(FmoeProblem), ctypes.c_void_p,
                                            ctypes.POINTER(FmoePlanView)]
         lib.fmoe_set_stage_events.argtypes = [ctypes.c_void_p]
+        lib.fmoe_selftest_wait_timeout.argtypes = [ctypes.c_uint64,
+                                                   ctypes.POINTER(ctypes.c_uint64),
+                                                   ctypes.c_void_p]
         lib.fmoe_forward_routed.argtypes = [ctypes.POINTER(FmoeProblem), ctypes.c_void_p,
                                             ctypes.c_void_p, ctypes.POINTER(FmoeTensors),
                                             ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
@@ -326,6 +329,22 @@ def read_device_error(prob: FmoeProblem, workspace: torch.Tensor) -> int:
     if rc != FMOE_OK:
         _raise(lib, rc, "read_device_error")
     return int(val.value)
+
+
+def selftest_wait_timeout(timeout_ns: int = 2_000_000, device=None) -> dict:
+    """Run the bounded-wait self-test kernel on the current stream: both of its waits can
+    never complete and must expire after ``timeout_ns``. Returns which expired and how
+    long each waited (ns); raises if the kernel itself failed."""
+    lib = load_library()
+    res = (ctypes.c_uint64 * 3)()
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = lib.fmoe_selftest_wait_timeout(int(timeout_ns), res, stream)
+    if rc != FMOE_OK:
+        _raise(lib, rc, "selftest_wait_timeout")
+    return {"expired_mask": int(res[0]), "mbarrier_wait_ns": int(res[1]),
+            "flag_wait_ns": int(res[2])}
 
 
 def plan_view(prob: FmoeProblem, workspace: torch.Tensor) -> dict:

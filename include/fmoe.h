@@ -130,6 +130,14 @@ int fmoe_read_device_error(const fmoe_problem* p, void* workspace, void* stream,
  * this one is live. */
 int fmoe_set_stage_events(void* const* events);
 
+/* Failure-detection self-test (no fault, trap or hang): runs a one-CTA kernel whose two
+ * bounded waits -- the mbarrier wait and the global-flag wait every GEMM kernel uses
+ * (the reference has no bounded waits; its failures surface as CUDA errors through
+ * kernel.cu:53-62) -- can never complete, with the limit set to timeout_ns (<= 1e8).
+ * Synchronises `stream`, then writes result[0] = bitmask of the waits that expired
+ * (bit 0 mbarrier, bit 1 flag; 3 when the limits work), result[1..2] = ns each waited. */
+int fmoe_selftest_wait_timeout(uint64_t timeout_ns, uint64_t* result, void* stream);
+
 /* Debug view of the permutation of the last call (device pointers into the workspace):
  * expert counts [E_local], expert offsets [E_local+1], row->token [row_cap],
  * (token,k)->row [T*top_k], and row_cap. For parity tests of the permute kernel. */
