@@ -21,7 +21,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/fmoe.h"
+#include "fmoe.h"
 #include "autotune_table.h"
 #include "fmoe_common.cuh"
 #include "fmoe_kernels.cuh"

@@ -25,7 +25,7 @@
 #include <mutex>
 #include <string>
 
-#include "../../include/fmoe.h"
+#include "fmoe.h"
 #include "autotune_table.h"
 #include "fmoe_common.cuh"
 #include "fmoe_kernels.cuh"

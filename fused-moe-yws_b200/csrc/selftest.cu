@@ -12,7 +12,7 @@
 
 #include <string>
 
-#include "../../include/fmoe.h"
+#include "fmoe.h"
 #include "fmoe_common.cuh"
 #include "fmoe_kernels.cuh"
 #include "sm100.cuh"
