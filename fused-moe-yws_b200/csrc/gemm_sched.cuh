@@ -75,28 +75,6 @@ struct Schedule {
   }
 };
 
-// A second walk of a CTA's schedule, kept ahead of the producer, that names the K steps
-// whose weight boxes get prefetched into L2.
-struct StepCursor {
-  Schedule sc;
-  int tile = -1, k = 0, k1 = 0;
-  __device__ __forceinline__ StepCursor(int n_tiles, int ks, int grid, int c)
-      : sc(n_tiles, ks, grid, c) {}
-  // advance to the next K step; false when the schedule is exhausted
-  __device__ __forceinline__ bool next() {
-    if (tile >= 0 && k + 1 < k1) {
-      ++k;
-      return true;
-    }
-    int t, a, b;
-    if (!sc.next(t, a, b)) return false;
-    tile = t;
-    k = a;
-    k1 = b;
-    return true;
-  }
-};
-
 // How a segment takes part in the fix-up of a split tile. Contributors are the CTAs
 // cf .. cl holding the tile's K steps in order.
 //   pair: exactly two contributors and ranges_cover_a_tile(): the head owner cf finishes

@@ -51,7 +51,6 @@ constexpr int kThreads = 320;
 constexpr int kSmemLimit = 232448;  // 227 KB opt-in dynamic shared memory per CTA
 constexpr int kEpiThreads = 256;    // warps 2..9
 constexpr int kBarAll = 3;          // named barrier id over all epilogue warps
-constexpr int kPrefetchSteps = 8;   // weight boxes prefetched into L2 ahead of the TMA loads
 
 template <int BN, bool kG1>
 struct Cfg {
@@ -292,25 +291,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     int it = 0, wseg = 0;
     bool ok = true;
     Schedule sched(num_tiles, KS, (int)gridDim.x, cta);
-    // L2 prefetch of the weight boxes kPrefetchSteps K steps ahead: the DRAM reads of the
-    // stream are in flight long before the TMA loads, which then hit L2
-    StepCursor pf(num_tiles, KS, (int)gridDim.x, cta);
-    int pf_tile = -1, pf_expert = 0;
-    bool pf_more = true;
-    auto prefetch_next = [&]() {
-      if (!pf_more || !(pf_more = pf.next())) return;
-      if (pf.tile != pf_tile) {
-        pf_tile = pf.tile;
-        pf_expert = args.chunks[pf_tile / args.m_tiles].expert;
-      }
-      const int pm = pf_tile % args.m_tiles;
-      if constexpr (kG1)
-        tma_prefetch_3d(&tmA, pf.k * 128, pm * 128, 2 * pf_expert);
-      else
-        tma_prefetch_2d(&tmA, pf.k * 128, pf_expert * args.H + pm * 256);
-    };
-    if (lane == 0)
-      for (int i = 0; i < kPrefetchSteps; ++i) prefetch_next();
     int tile, k0, k1;
     while (ok && sched.next(tile, k0, k1)) {
       const Chunk ch = args.chunks[tile / args.m_tiles];
@@ -368,7 +348,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(&sfull[slot], ch.ncols * 4);
           bulk_load_1d(sring + slot * BN, asrc + (int64_t)ks * args.row_cap, ch.ncols * 4,
                        &sfull[slot]);
-          if (kPrefetchSteps > 0) prefetch_next();
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);

@@ -35,7 +35,6 @@ constexpr int kTmThreads = 576;     // 18 warps
 constexpr int kTmEpiThreads = 512;  // warps 2..17
 constexpr int kTmBarAll = 1;        // named barrier over the epilogue warps
 constexpr int kTmSmemLimit = 232448;
-constexpr int kTmPrefetchSteps = 8;  // weight boxes prefetched into L2 ahead of the TMA loads
 
 template <bool kG1>
 struct TmCfg {
@@ -196,29 +195,6 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     int it = 0, wseg = 0;
     bool ok = true;
     Schedule sched(num_tiles, KS, (int)gridDim.x, cta);
-    // L2 prefetch of the weight boxes kTmPrefetchSteps K steps ahead
-    StepCursor pf(num_tiles, KS, (int)gridDim.x, cta);
-    int pf_tile = -1, pf_expert = 0;
-    bool pf_more = true;
-    auto prefetch_next = [&]() {
-      if (!pf_more || !(pf_more = pf.next())) return;
-      if (pf.tile != pf_tile) {
-        pf_tile = pf.tile;
-        pf_expert = args.chunks[pf_tile / args.m_tiles].expert;
-      }
-      const int pm = pf_tile % args.m_tiles;
-      if constexpr (kG1) {
-        const int wrow = pf_expert * 2 * args.I + pm * 128;
-        tma_prefetch_2d(&tmB, pf.k * 128, wrow);
-        tma_prefetch_2d(&tmB, pf.k * 128, wrow + args.I);
-      } else {
-        const int wrow = pf_expert * args.H + pm * 256;
-        tma_prefetch_2d(&tmB, pf.k * 128, wrow);
-        tma_prefetch_2d(&tmB, pf.k * 128, wrow + 128);
-      }
-    };
-    if (lane == 0)
-      for (int i = 0; i < kTmPrefetchSteps; ++i) prefetch_next();
     int tile, k0, k1;
     while (ok && sched.next(tile, k0, k1)) {
       const Chunk ch = args.chunks[tile / args.m_tiles];
@@ -281,7 +257,6 @@ __global__ void __launch_bounds__(kTmThreads, 1)
           mbar_arrive_expect_tx(&sfull[slot], ch.ncols * 4);
           bulk_load_1d(sring + slot * 128, asrc + (int64_t)ks * args.row_cap, ch.ncols * 4,
                        &sfull[slot]);
-          if (kTmPrefetchSteps > 0) prefetch_next();
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
