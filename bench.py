@@ -471,7 +471,28 @@ def run_reference(args, rank):
     return base
 
 
+# The JSON line is the only thing this script writes to stdout. Libraries loaded later
+# (NCCL prints its version there, for one) write to the process's file descriptor 1 from
+# C, so descriptor 1 is pointed at stderr and the result goes to a duplicate of the
+# original stdout.
+_RESULT_OUT = None
+
+
+def _claim_stdout():
+    global _RESULT_OUT
+    if _RESULT_OUT is None:
+        sys.stdout.flush()
+        _RESULT_OUT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
+
+
+def emit(line: dict) -> None:
+    _RESULT_OUT.write(json.dumps(line) + "\n")
+    _RESULT_OUT.flush()
+
+
 def main():
+    _claim_stdout()
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=30)
@@ -500,7 +521,7 @@ def main():
     if args.impl == "reference":
         line = run_reference(args, rank)
         if line is not None:
-            print(json.dumps(line), flush=True)
+            emit(line)
         if world > 1:
             dist.destroy_process_group()
         return
@@ -508,7 +529,7 @@ def main():
     if world > 1:
         line = run_ep(args, world, rank, local)
         if rank == 0:
-            print(json.dumps(line), flush=True)
+            emit(line)
         dist.barrier()
         dist.destroy_process_group()
         return
@@ -597,7 +618,7 @@ def main():
             line["sweep"] = sweep(args.seed, hbm_peak, fp8_peak,
                                   tiles=tuple(int(x) for x in args.sweep_tiles.split(",")))
             line["sweep_fp8_peak_tflops"] = fp8_peak
-        print(json.dumps(line), flush=True)
+        emit(line)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
