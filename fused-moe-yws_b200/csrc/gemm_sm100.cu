@@ -90,7 +90,8 @@ struct Cfg {
   static_assert(kNBuf >= 2, "need at least two accumulator buffers");
 };
 
-__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+// fast division: the reference is built with --use_fast_math, which approximates it too
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 __device__ __forceinline__ void set_error(int* err, volatile int* abort_flag, int code) {
   atomicOr(err, code);

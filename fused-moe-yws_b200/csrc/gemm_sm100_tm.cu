@@ -60,7 +60,8 @@ struct TmCfg {
   static_assert((16 + 16 + 2 + 2 + 4 + 2 * kMaxSlots + 3) * 8 <= kBarBytes, "barrier area");
 };
 
-__device__ __forceinline__ float silu_tm(float x) { return x / (1.0f + __expf(-x)); }
+// fast division: the reference is built with --use_fast_math, which approximates it too
+__device__ __forceinline__ float silu_tm(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 template <int N>
 __device__ __forceinline__ void promote_tm(float (&acc)[N], uint32_t taddr, float s) {
