@@ -57,21 +57,29 @@ struct TmCfg {
   static constexpr int kPartialFloats = 128 * 256;
   static_assert(kStages >= 2, "pipeline depth");
   static_assert(kSmemBytes <= kTmSmemLimit, "shared memory budget");
-  static_assert((16 + 16 + 2 + 2 + 4 + 2 * kMaxSlots + 3) * 8 <= kBarBytes, "barrier area");
+  static_assert((16 + 16 + 2 + 2 + 4 + 2 * kMaxSlots + 4 + 4) * 8 <= kBarBytes, "barrier area");
 };
 
 // fast division: the reference is built with --use_fast_math, which approximates it too
 __device__ __forceinline__ float silu_tm(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
+// acc[i] += D[i] * s, 16 TMEM columns per load (the thread's 64 accumulators leave room
+// for 16 loaded values), as packed FMAs (each lane of fma.rn.f32x2 rounds like fmaf).
 template <int N>
 __device__ __forceinline__ void promote_tm(float (&acc)[N], uint32_t taddr, float s) {
+  const float2 s2 = make_float2(s, s);
 #pragma unroll
   for (int c = 0; c < N / 16; ++c) {
     uint32_t v[16];
     tmem_ld_32x32b<16>(taddr + c * 16, v);
     tmem_ld_wait();
 #pragma unroll
-    for (int i = 0; i < 16; ++i) acc[c * 16 + i] = fmaf(__uint_as_float(v[i]), s, acc[c * 16 + i]);
+    for (int i = 0; i < 16; i += 2) {
+      const float2 r = __ffma2_rn(make_float2(__uint_as_float(v[i]), __uint_as_float(v[i + 1])),
+                                  s2, make_float2(acc[c * 16 + i], acc[c * 16 + i + 1]));
+      acc[c * 16 + i] = r.x;
+      acc[c * 16 + i + 1] = r.y;
+    }
   }
 }
 
@@ -145,6 +153,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(mma_done + 2);
   volatile int* last_flag = abort_flag + 1;
+  // segment descriptors {tile, k0, k1, -} beside the 2-slot weight-scale ring: the producer
+  // walks the schedule and publishes each segment with its scales (tile < 0: no more work),
+  // so the epilogue warps hold no schedule state in registers
+  int4* segd = reinterpret_cast<int4*>(mma_done + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
@@ -228,6 +240,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
           dst[i] = __ldg(g + i);
           dst[kMaxKSteps + i] = __ldg(u + i);
         }
+        if (lane == 0) segd[ws] = make_int4(tile, k0, k1, 0);
         mbar_arrive(&wfull[ws]);  // every lane: its stores are released by its own arrive
         ++wseg;
       }
@@ -261,6 +274,17 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
+    }
+    if (ok) {
+      // end of work for the epilogue
+      const int ws = wseg & 1;
+      bool w_ok = true;
+      if (lane == 0) w_ok = mbar_wait(&wempty[ws], ((wseg >> 1) & 1) ^ 1, abort_flag);
+      ok = __shfl_sync(0xffffffffu, w_ok, 0);
+      if (ok) {
+        if (lane == 0) segd[ws] = make_int4(-1, 0, 0, 0);
+        mbar_arrive(&wfull[ws]);
+      }
     }
     if (lane == 0) {
       if (!ok) {
@@ -337,14 +361,22 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     float acc_u[kG1 ? 32 : 1];
     int it = 0, wseg = 0;
     bool ok = true;
-    Schedule sched(num_tiles, KS, (int)gridDim.x, cta);
-    int tile, k0, k1;
-    while (sched.next(tile, k0, k1)) {
-      const Chunk ch = args.chunks[tile / args.m_tiles];
-      const int m = tile % args.m_tiles;
-      // weight-scale rows of this tile, staged by the producer into the 2-slot ring
+    for (;;) {
+      // next segment and its weight-scale rows, staged by the producer into the 2-slot ring;
+      // one decision for all epilogue warps (nobody waits at a barrier alone)
       const int ws = wseg & 1;
-      if (ok && !mbar_wait(&wfull[ws], (wseg >> 1) & 1, abort_flag)) ok = false;
+      const bool have = mbar_wait(&wfull[ws], (wseg >> 1) & 1, abort_flag);
+      if (named_bar_or(kTmBarAll, kTmEpiThreads, !have)) {
+        ok = have;
+        break;
+      }
+      int k0, k1;
+      {
+        const int4 d = segd[ws];
+        if (d.x < 0) break;  // no more work
+        k0 = d.y;
+        k1 = d.z;
+      }
       const float* wrow = wsc + ws * 2 * kMaxKSteps;
 #pragma unroll
       for (int i = 0; i < NA; ++i) acc[i] = 0.0f;
@@ -352,8 +384,12 @@ __global__ void __launch_bounds__(kTmThreads, 1)
 #pragma unroll
         for (int i = 0; i < 32; ++i) acc_u[i] = 0.0f;
       }
-      const SplitRole role = split_role(sched, tile, k0, k1);
-      if (role.split && role.pair && role.head) {
+      {
+        // the descriptor fields are re-read from shared memory where needed, so no
+        // schedule state stays live across the K loop
+        const Schedule sc(num_tiles, KS, (int)gridDim.x, cta);
+        const SplitRole role = split_role(sc, segd[ws].x, k0, k1);
+        if (role.split && role.pair && role.head) {
         // start from the tail owner's partial (see SplitRole)
         bool ready = true;
         if (tid_e == 0 && ok) ready = wait_nonzero(args.tile_counters + role.cf, abort_flag);
@@ -372,6 +408,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
             load_vec<64>(acc, pp + 64 * j);
           }
         }
+      }
       }
       for (int ks = k0; ks < k1; ++ks, ++it) {
         const int b = it % NB, use = it / NB;
@@ -398,7 +435,9 @@ __global__ void __launch_bounds__(kTmThreads, 1)
           mbar_arrive(&sempty[slot]);
         }
       }
-      // the weight-scale slot is free again once this warp's promotions are done
+      // the weight-scale slot (and its descriptor) is free again once this warp's
+      // promotions are done
+      const int tile = segd[ws].x;
       __syncwarp();
       if (lane == 0 && ok) mbar_arrive(&wempty[ws]);
       ++wseg;
@@ -407,6 +446,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         ok = false;
         break;
       }
+      const Schedule sched(num_tiles, KS, (int)gridDim.x, cta);
+      const SplitRole role = split_role(sched, tile, k0, k1);
+      const Chunk ch = args.chunks[tile / args.m_tiles];
+      const int m = tile % args.m_tiles;
       // ---- stream-K partial tiles ([row][256] fp32), finished by the last contributor ----
       if (role.split && role.pair) {
         if (!role.head) {

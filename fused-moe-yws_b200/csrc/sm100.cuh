@@ -56,20 +56,37 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
   return ok != 0;
 }
 
+// try_wait that lets the hardware suspend the thread until the phase completes, for at
+// most hint_ns: a waiting warp takes no issue slots from the warps that share its SM
+// sub-partition (a spinning MMA issuer or TMA producer measurably slowed the epilogue
+// warps beside it).
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t bar_addr, uint32_t parity,
+                                                      uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+constexpr uint32_t kSuspendHintNs = 20000;  // 20 us: bounds the abort / timeout checks' delay
+
 // Wait for the phase with the given parity to complete. Returns false on timeout or
-// when *abort becomes non-zero (another role gave up), never spins forever.
+// when *abort becomes non-zero (another role gave up), never waits forever.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
                                           const volatile int* abort,
                                           uint64_t timeout_ns = kWaitTimeoutNs) {
   const uint32_t a = smem_addr(bar);
   if (mbar_try_wait(a, parity)) return true;
-  uint64_t t0 = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(a, parity)) return true;
-    if ((i & 63) == 0) {
-      if (*abort) return false;
-      if (globaltimer() - t0 > timeout_ns) return false;
-    }
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+    if (mbar_try_wait_suspend(a, parity, kSuspendHintNs)) return true;
+    if (*abort) return false;
+    if (globaltimer() - t0 > timeout_ns) return false;
   }
 }
 
