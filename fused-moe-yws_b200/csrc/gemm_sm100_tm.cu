@@ -537,11 +537,12 @@ __global__ void __launch_bounds__(kTmThreads, 1)
             hi[k / 4] = (uint32_t)h01 | ((uint32_t)h23 << 16);
             lo[k / 4] = (uint32_t)l01 | ((uint32_t)l23 << 16);
           }
+          // full 32-byte sectors (the workspace is 256-byte aligned, 2I a multiple of 256):
+          // 16-byte stores scattered over 32 rows per instruction stalled the epilogue for
+          // microseconds per tile while the TMA loads saturated the memory system
           uint8_t* dst = args.cq + grow * (2 * (int64_t)args.I) + m * 256 + j * 32;
-          reinterpret_cast<uint4*>(dst)[0] = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-          reinterpret_cast<uint4*>(dst)[1] = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-          reinterpret_cast<uint4*>(dst + 128)[0] = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-          reinterpret_cast<uint4*>(dst + 128)[1] = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+          st_global_v8(dst, hi);
+          st_global_v8(dst + 128, lo);
           if (j == 0) args.c_scale[(int64_t)m * args.row_cap + grow] = amax / 448.0f;
         }
         named_bar(kTmBarAll, kTmEpiThreads);  // ax is reused by the next tile
@@ -549,15 +550,18 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         // ---- weighted expert output: 64 consecutive bf16 of this token row ----
         if (real) {
           const float w = __ldg(args.row_w + grow);
-          uint4* dst = reinterpret_cast<uint4*>(args.ow + grow * args.H + m * 256 + 64 * j);
+          // 32-byte stores: full sectors (H is a multiple of 256 on this path)
+          __nv_bfloat16* dst = args.ow + grow * args.H + m * 256 + 64 * j;
 #pragma unroll
-          for (int v = 0; v < 8; ++v) {
-            uint4 o;
-            __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+          for (int v = 0; v < 4; ++v) {
+            uint32_t o[8];
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
-              oh[u] = __floats2bfloat162_rn(acc[8 * v + 2 * u] * w, acc[8 * v + 2 * u + 1] * w);
-            dst[v] = o;
+            for (int u = 0; u < 8; ++u) {
+              const __nv_bfloat162 h =
+                  __floats2bfloat162_rn(acc[16 * v + 2 * u] * w, acc[16 * v + 2 * u + 1] * w);
+              o[u] = *reinterpret_cast<const uint32_t*>(&h);
+            }
+            st_global_v8(dst + 16 * v, o);
           }
         }
       }
