@@ -276,7 +276,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  pdl_wait();     // the permute / GEMM1 outputs of the previous kernel are now visible
+  // The producer warp waits for the previous kernel only once its first weight boxes are
+  // in flight (below); every other warp waits here, before touching its outputs.
+  if (warp != 0) pdl_wait();  // the permute / GEMM1 outputs of the previous kernel are visible
   pdl_trigger();  // let the next kernel's CTAs start their prologue as SMs free up
 
   const int num_tiles = args.meta[kMetaNumChunks] * args.m_tiles;
@@ -289,8 +291,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // up rows of W13) into a 2-slot shared ring; lane 0 alone issues the copies.
     const uint64_t pol_w = policy_evict_first();  // weights: streamed once
     const uint64_t pol_a = policy_evict_last();   // token tiles: re-read by every m tile
-    int it = 0, wseg = 0;
-    bool ok = true;
+    // The chunk list and the weights do not depend on the previous kernel: the routing plan
+    // was complete before it could start this grid (it triggers only after its own
+    // dependency wait). So the weight boxes of the first min(S, steps) stages are issued
+    // before griddepcontrol.wait, overlapping the pipeline's first HBM latency with the
+    // previous kernel's tail; the token tiles and their scales follow after the wait.
+    int it = 0, wseg = 0, pre = 0;
+    bool ok = true, waited = false;
     Schedule sched(num_tiles, KS, (int)gridDim.x, cta);
     int tile, k0, k1;
     while (ok && sched.next(tile, k0, k1)) {
@@ -324,6 +331,27 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(&wfull[ws]);  // every lane: its stores are released by its own arrive
         ++wseg;
       }
+      // weight box of K step ks into stage s (the stage's full barrier expects the token
+      // tile too)
+      auto load_weights = [&](int s, int ks) {
+        uint8_t* sa = stages + s * C::kStageBytes;
+        mbar_arrive_expect_tx(&full[s], C::kTx);
+        if constexpr (kG1) {
+          // {K, row in half, (expert, gate|up)} box {128, 128, 2}: gate tile, then up tile
+          tma_load_3d(sa, &tmA, &full[s], ks * 128, m * 128, 2 * ch.expert, pol_w);
+        } else {
+          // 256 W2 rows
+          tma_load_2d(sa, &tmA, &full[s], ks * 128, ch.expert * args.H + m * 256, pol_w);
+        }
+      };
+      if (!waited) {
+        if (lane == 0) {
+          pre = k1 - k0 < S ? k1 - k0 : S;  // stages are fresh: no empty wait needed
+          for (int i = 0; i < pre; ++i) load_weights(i, k0 + i);
+        }
+        pdl_wait();
+        waited = true;
+      }
       if (lane == 0) {
         const float* asrc = args.act_scale + ch.row0;
         for (int ks = k0; ks < k1; ++ks, ++it) {
@@ -333,16 +361,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          uint8_t* sa = stages + s * C::kStageBytes;
-          uint8_t* sb = sa + C::kABytes;
-          mbar_arrive_expect_tx(&full[s], C::kTx);
+          uint8_t* sb = stages + s * C::kStageBytes + C::kABytes;
+          if (it >= pre) load_weights(s, ks);
           if constexpr (kG1) {
-            // {K, row in half, (expert, gate|up)} box {128, 128, 2}: gate tile, then up tile
-            tma_load_3d(sa, &tmA, &full[s], ks * 128, m * 128, 2 * ch.expert, pol_w);
             tma_load_2d(sb, &tmB, &full[s], ks * 128, ch.row0, pol_a);
           } else {
-            // 256 W2 rows; {byte in block, row, 128-byte block} box {128, BN, 2}: hi, then lo
-            tma_load_2d(sa, &tmA, &full[s], ks * 128, ch.expert * args.H + m * 256, pol_w);
+            // {byte in block, row, 128-byte block} box {128, BN, 2}: hi, then lo
             tma_load_3d(sb, &tmB, &full[s], 0, ch.row0, 2 * ks, pol_a);
           }
           // activation / intermediate scales of this K step for the chunk's columns
@@ -353,6 +377,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
     }
+    if (!waited) pdl_wait();  // no work: still ordered after the previous kernel
     if (lane == 0) {
       if (!ok) set_error(args.err, abort_flag, kErrTimeoutProducer);
       // drain: every issued copy must land before the CTA's shared memory is released
