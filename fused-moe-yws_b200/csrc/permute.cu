@@ -21,6 +21,8 @@ namespace fmoe {
 namespace {
 constexpr int kTok = kRouteTokensPerCta;
 constexpr int kMaxEntries = kTok * 32;
+constexpr int kPreVec = 512;          // 16-byte row vectors prefetched per CTA (8 KB)
+constexpr int kPreScales = kTok * 64;  // block scales prefetched per CTA (4 KB)
 
 __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
   uint4 v;
@@ -42,10 +44,37 @@ __global__ void __launch_bounds__(256) scatter_gather_kernel(ScatterArgs a) {
   __shared__ int s_wn[kW];
   __shared__ int s_nlocal;
 
+  __shared__ uint4 s_pre[kPreVec];     // [token][vector] of this CTA's column slice
+  __shared__ float s_pscale[kPreScales];  // [token][block]
+
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t lt = (1u << lane) - 1u;
   const int K = a.top_k, nent = kTok * K;
   const int64_t t0 = (int64_t)blockIdx.x * kTok;
+  // this CTA copies 16-byte column vectors [v0, v1) of every local row
+  const int vpr = a.H / 16;
+  const int v0 = (int)((int64_t)vpr * blockIdx.y / gridDim.y);
+  const int v1 = (int)((int64_t)vpr * (blockIdx.y + 1) / gridDim.y);
+  const int vw = v1 - v0;
+  const int kb = a.H / kBlock;
+  // The source rows and their scales were complete before the routing kernel passed its
+  // own dependency wait (this grid starts only after that), so they are fetched before
+  // this kernel's wait: the HBM latency of the copy overlaps the routing kernel instead
+  // of following it. Only small slices are prefetched (decode-sized batches).
+  const bool pre_rows = kTok * vw <= kPreVec;
+  const bool pre_scales = blockIdx.y == 0 && kTok * kb <= kPreScales;
+  if (pre_rows) {
+    for (int v = tid; v < kTok * vw; v += blockDim.x) {
+      const int64_t t = t0 + v / vw;
+      if (t < a.T) s_pre[v] = ld_nc_v4(a.hidden + t * a.H + (v0 + v % vw) * 16);
+    }
+  }
+  if (pre_scales) {
+    for (int v = tid; v < kTok * kb; v += blockDim.x) {
+      const int64_t t = t0 + v / kb;
+      if (t < a.T) s_pscale[v] = __ldg(a.hidden_scale + (int64_t)(v % kb) * a.T + t);
+    }
+  }
   pdl_wait();
   pdl_trigger();
   // every global index load of the CTA is issued in this one phase
@@ -113,25 +142,21 @@ __global__ void __launch_bounds__(256) scatter_gather_kernel(ScatterArgs a) {
     __syncthreads();
   }
   const int n = s_nlocal;
-  // this CTA copies 16-byte column vectors [v0, v1) of every local row
-  const int vpr = a.H / 16;
-  const int v0 = (int)((int64_t)vpr * blockIdx.y / gridDim.y);
-  const int v1 = (int)((int64_t)vpr * (blockIdx.y + 1) / gridDim.y);
-  const int vw = v1 - v0;
   for (int v = tid; v < n * vw; v += blockDim.x) {
-    const int li = v / vw, part = v0 + (v - li * vw);
+    const int li = v / vw, pv = v - li * vw;
     const int i = s_list[li];
-    const int64_t t = t0 + i / K;
-    const uint4 x = ld_nc_v4(a.hidden + t * a.H + part * 16);
-    *reinterpret_cast<uint4*>(a.a_perm + (int64_t)s_row[i] * a.H + part * 16) = x;
+    const int tok = i / K;
+    const uint4 x = pre_rows ? s_pre[tok * vw + pv]
+                             : ld_nc_v4(a.hidden + (t0 + tok) * a.H + (v0 + pv) * 16);
+    *reinterpret_cast<uint4*>(a.a_perm + (int64_t)s_row[i] * a.H + (v0 + pv) * 16) = x;
   }
-  const int kb = a.H / kBlock;
   if (blockIdx.y == 0) {
     for (int v = tid; v < n * kb; v += blockDim.x) {
       const int li = v / kb, b = v - li * kb;
       const int i = s_list[li];
-      const int64_t t = t0 + i / K;
-      a.a_scale[(int64_t)b * a.row_cap + s_row[i]] = a.hidden_scale[(int64_t)b * a.T + t];
+      const int tok = i / K;
+      a.a_scale[(int64_t)b * a.row_cap + s_row[i]] =
+          pre_scales ? s_pscale[tok * kb + b] : a.hidden_scale[(int64_t)b * a.T + t0 + tok];
     }
   }
   // padding rows of the experts this CTA column owns (expert e goes to x = e % gridDim.x)
