@@ -28,7 +28,7 @@ NVCC = str(CUDA_HOME / "bin" / "nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
               f"-I{INCLUDE}", "-Xptxas", "-v"]
-CU_SOURCES = ["route.cu", "permute.cu", "gemm_sm100.cu", "gemm_sm100_tm.cu", "fmoe_api.cu",
+CU_SOURCES = ["route.cu", "permute.cu", "gemm_sm100.cu", "gemm_sm100_tm.cu", "fmoe_api.cu", "ep.cu",
               "route_static.cu", "selftest.cu"]
 
 

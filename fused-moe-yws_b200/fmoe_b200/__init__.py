@@ -32,7 +32,8 @@ FMOE_OK, FMOE_ERR_VALUE, FMOE_ERR_TYPE, FMOE_ERR_RUNTIME, FMOE_ERR_WORKSPACE, FM
 EXPORTED_SYMBOLS = ("fmoe_abi_version", "fmoe_last_error", "fmoe_validate", "fmoe_workspace_size",
                     "fmoe_autotune_tile_n", "fmoe_forward", "fmoe_route", "fmoe_read_device_error",
                     "fmoe_plan_view_get", "fmoe_set_stage_events", "fmoe_route_static",
-                    "fmoe_forward_routed", "fmoe_selftest_wait_timeout")
+                    "fmoe_forward_routed", "fmoe_selftest_wait_timeout", "fmoe_ep_plan",
+                    "fmoe_ep_pack", "fmoe_ep_unpack", "fmoe_ep_combine")
 
 
 class FmoeProblem(ctypes.Structure):
@@ -97,6 +98,11 @@ def load_library(path: Path | str | None = None):
         lib.fmoe_forward_routed.argtypes = [ctypes.POINTER(FmoeProblem), ctypes.c_void_p,
                                             ctypes.c_void_p, ctypes.POINTER(FmoeTensors),
                                             ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+        vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+        lib.fmoe_ep_plan.argtypes = [vp, i64, i32, i32, i32, vp, vp, vp, vp]
+        lib.fmoe_ep_pack.argtypes = [vp, vp, vp, vp, vp, i64, i32, i32, i32, vp, vp]
+        lib.fmoe_ep_unpack.argtypes = [vp, i64, i32, i32, vp, vp, vp, vp, vp]
+        lib.fmoe_ep_combine.argtypes = [vp, vp, i64, i32, i32, vp, vp]
         for name in EXPORTED_SYMBOLS:
             if not hasattr(lib, name):
                 raise RuntimeError(f"{p} does not export {name}")
@@ -317,6 +323,75 @@ def route(routing_logits: torch.Tensor, routing_bias: torch.Tensor, n_group: int
     if rc != FMOE_OK:
         _raise(lib, rc, "route")
     return idx, w
+
+
+# ---- expert-parallel exchange, device side (include/fmoe.h fmoe_ep_*) ----------------------
+def ep_payload_bytes(H: int, K: int) -> int:
+    """Bytes of one exchange row: FP8 row | block scales | expert ids | weights."""
+    return H + 4 * (H // 128) + 8 * K
+
+
+def _stream(dev):
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def ep_plan(topk_idx: torch.Tensor, world: int, experts_per_rank: int):
+    """Send plan: (pos int32 [world, T], tokens int32 [sum], counts int32 [world])."""
+    T, K = topk_idx.shape
+    dev = topk_idx.device
+    lib = load_library()
+    pos = torch.empty(world, T, dtype=torch.int32, device=dev)
+    tokens = torch.empty(max(T * world, 1), dtype=torch.int32, device=dev)
+    counts = torch.empty(world, dtype=torch.int32, device=dev)
+    rc = lib.fmoe_ep_plan(topk_idx.data_ptr(), T, K, world, experts_per_rank, pos.data_ptr(),
+                          tokens.data_ptr(), counts.data_ptr(), _stream(dev))
+    if rc != FMOE_OK:
+        _raise(lib, rc, "ep_plan")
+    return pos, tokens, counts
+
+
+def ep_pack(hidden_states, hidden_states_scale, topk_idx, topk_w, pos, rows: int):
+    """Exchange rows for every (token, rank) of the plan, [rows, payload] uint8."""
+    T, H = hidden_states.shape
+    K = topk_idx.shape[1]
+    dev = hidden_states.device
+    lib = load_library()
+    send = torch.empty(rows, ep_payload_bytes(H, K), dtype=torch.uint8, device=dev)
+    rc = lib.fmoe_ep_pack(hidden_states.data_ptr(), hidden_states_scale.data_ptr(),
+                          topk_idx.data_ptr(), topk_w.data_ptr(), pos.data_ptr(), T, H, K,
+                          pos.shape[0], send.data_ptr(), _stream(dev))
+    if rc != FMOE_OK:
+        _raise(lib, rc, "ep_pack")
+    return send
+
+
+def ep_unpack(recv: torch.Tensor, H: int, K: int):
+    """Received rows -> (hidden fp8 [R, H], scale fp32 [H/128, R], idx int32, w fp32)."""
+    R = recv.shape[0]
+    dev = recv.device
+    lib = load_library()
+    hs = torch.empty(R, H, dtype=torch.float8_e4m3fn, device=dev)
+    sc = torch.empty(H // 128, R, dtype=torch.float32, device=dev)
+    idx = torch.empty(R, K, dtype=torch.int32, device=dev)
+    w = torch.empty(R, K, dtype=torch.float32, device=dev)
+    rc = lib.fmoe_ep_unpack(recv.data_ptr(), R, H, K, hs.data_ptr(), sc.data_ptr(),
+                            idx.data_ptr(), w.data_ptr(), _stream(dev))
+    if rc != FMOE_OK:
+        _raise(lib, rc, "ep_unpack")
+    return hs, sc, idx, w
+
+
+def ep_combine(back: torch.Tensor, pos: torch.Tensor, T: int):
+    """Per token, its returned partial rows summed in fp32 in rank order -> bf16 [T, H]."""
+    H = back.shape[1]
+    dev = back.device
+    lib = load_library()
+    out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    rc = lib.fmoe_ep_combine(back.data_ptr(), pos.data_ptr(), T, H, pos.shape[0],
+                             out.data_ptr(), _stream(dev))
+    if rc != FMOE_OK:
+        _raise(lib, rc, "ep_combine")
+    return out
 
 
 def read_device_error(prob: FmoeProblem, workspace: torch.Tensor) -> int:

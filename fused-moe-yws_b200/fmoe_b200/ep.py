@@ -18,6 +18,12 @@ GPU over `torch.distributed` (NCCL on B200s, gloo for the CPU tests):
 
 The token order inside every message is ascending token id, so dispatch, compute and
 combine are all deterministic.
+
+On CUDA the send plan, the payload packing and unpacking and the rank-ordered combine are
+kernels of the library (`fmoe_ep_*` in include/fmoe.h: one launch each, instead of chains
+of framework ops); only the counts cross to the host, because NCCL's all-to-all-v takes
+its split sizes there. The framework-op version below is the CPU restatement the gloo
+tests exercise, and `fused_exchange=False` selects it on CUDA too.
 """
 from __future__ import annotations
 
@@ -70,7 +76,7 @@ class ExpertParallelMoE:
     def __init__(self, num_experts: int = 256, n_group: int = 8, topk_group: int = 4,
                  top_k: int = 8, routed_scaling_factor: float = 2.5, group=None,
                  weights: Optional[dict] = None, route_fn: Optional[RouteFn] = None,
-                 local_fn: Optional[LocalFn] = None):
+                 local_fn: Optional[LocalFn] = None, fused_exchange: bool = True):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -85,6 +91,7 @@ class ExpertParallelMoE:
         self.route_fn = route_fn or self._route_gpu
         self.local_fn = local_fn or self._local_gpu
         self.timings = EPTimings()
+        self.fused_exchange = fused_exchange
 
     # ---- default B200 implementations --------------------------------------------------
     def _route_gpu(self, logits, bias):
@@ -122,15 +129,22 @@ class ExpertParallelMoE:
         idx = idx.to(torch.int32).contiguous()
         w = w.to(torch.float32).contiguous()
         mark()
-        # destinations: rank owning each selected expert (unselected slots are -1)
-        owner = torch.where(idx >= 0, idx // self.e_per_rank, torch.full_like(idx, -1))
-        mask = torch.zeros(T, self.world, dtype=torch.bool, device=dev)
-        valid = owner >= 0
-        rows = torch.arange(T, device=dev).unsqueeze(1).expand(T, K)
-        mask[rows[valid], owner[valid].long()] = True
-        send_counts = mask.sum(0).to(torch.int64)
-        order = torch.nonzero(mask.t(), as_tuple=False)  # (dest, token), sorted by dest, token
-        tokens = order[:, 1]
+        fused = self.fused_exchange and dev.type == "cuda"
+        if fused:
+            import fmoe_b200
+
+            pos, _, counts = fmoe_b200.ep_plan(idx, self.world, self.e_per_rank)
+            send_counts = counts.to(torch.int64)
+        else:
+            # destinations: rank owning each selected expert (unselected slots are -1)
+            owner = torch.where(idx >= 0, idx // self.e_per_rank, torch.full_like(idx, -1))
+            mask = torch.zeros(T, self.world, dtype=torch.bool, device=dev)
+            valid = owner >= 0
+            rows = torch.arange(T, device=dev).unsqueeze(1).expand(T, K)
+            mask[rows[valid], owner[valid].long()] = True
+            send_counts = mask.sum(0).to(torch.int64)
+            order = torch.nonzero(mask.t(), as_tuple=False)  # (dest, token), by dest, token
+            tokens = order[:, 1]
         recv_counts = torch.empty_like(send_counts)
         if self.world > 1:
             dist.all_to_all_single(recv_counts, send_counts, group=self.group)
@@ -138,29 +152,39 @@ class ExpertParallelMoE:
             recv_counts.copy_(send_counts)
         send_splits = send_counts.tolist()
         recv_splits = recv_counts.tolist()
-        payload = pack_rows(hidden_states, hidden_states_scale, idx, w, tokens)
+        if fused:
+            payload = fmoe_b200.ep_pack(hidden_states, hidden_states_scale, idx, w, pos,
+                                        sum(send_splits))
+        else:
+            payload = pack_rows(hidden_states, hidden_states_scale, idx, w, tokens)
         recv = torch.empty(sum(recv_splits), payload.shape[1], dtype=torch.uint8, device=dev)
         if self.world > 1:
             dist.all_to_all_single(recv, payload, recv_splits, send_splits, group=self.group)
         else:
             recv.copy_(payload)
-        hs_r, sc_r, idx_r, w_r = unpack_rows(recv, H, K)
+        if fused:
+            hs_r, sc_r, idx_r, w_r = fmoe_b200.ep_unpack(recv, H, K)
+        else:
+            hs_r, sc_r, idx_r, w_r = unpack_rows(recv, H, K)
         mark()
         part = self.local_fn(idx_r, w_r, hs_r, sc_r, self.local_offset)
         mark()
-        back = torch.empty(len(tokens), H, dtype=torch.bfloat16, device=dev)
+        back = torch.empty(sum(send_splits), H, dtype=torch.bfloat16, device=dev)
         if self.world > 1:
             dist.all_to_all_single(back, part.contiguous(), send_splits, recv_splits,
                                    group=self.group)
         else:
             back.copy_(part)
-        out = torch.zeros(T, H, dtype=torch.float32, device=dev)
-        start = 0
-        for n in send_splits:  # rank order: each token's partials are added in a fixed order
-            if n:
-                out.index_add_(0, tokens[start:start + n], back[start:start + n].float())
-            start += n
-        res = out.to(torch.bfloat16)
+        if fused:
+            res = fmoe_b200.ep_combine(back, pos, T)
+        else:
+            out = torch.zeros(T, H, dtype=torch.float32, device=dev)
+            start = 0
+            for n in send_splits:  # rank order: each token's partials are added in order
+                if n:
+                    out.index_add_(0, tokens[start:start + n], back[start:start + n].float())
+                start += n
+            res = out.to(torch.bfloat16)
         mark()
         if timed and len(ev) == 5:
             torch.cuda.synchronize()

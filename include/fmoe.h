@@ -164,6 +164,40 @@ int fmoe_plan_view_get(const fmoe_problem* p, void* workspace, fmoe_plan_view* v
 int fmoe_route_static(const fmoe_problem* p, const float* routing_logits,
                       const void* routing_bias, const fmoe_route_out* out, void* stream);
 
+/* Expert-parallel exchange, device side. The reference operator computes one expert slice
+ * (local_expert_offset, kernel.cu:540-544) and leaves the exchange of tokens and partial
+ * outputs between GPUs to its caller; these entry points build what that caller sends and
+ * consume what it receives (the collectives themselves are the caller's, e.g. NCCL
+ * all-to-all). Rank d owns experts [d * experts_per_rank, (d + 1) * experts_per_rank); a
+ * token goes once to every rank owning one of its selected experts. All pointers are device
+ * pointers; work is queued on `stream`.
+ *
+ * Payload row (bytes): FP8 hidden row [H] | block scales fp32 [H/128] | expert ids int32
+ * [top_k] | weights fp32 [top_k]; rows are packed back to back.
+ *
+ * fmoe_ep_plan: pos [world, T] = send-buffer row of (token, rank) or -1; tokens [sum counts]
+ *   = token of each send row; counts [world] = rows per rank. Rows are grouped by rank in
+ *   rank order, tokens ascending inside a group. */
+int fmoe_ep_plan(const int* topk_idx, int64_t num_tokens, int top_k, int world,
+                 int experts_per_rank, int* pos, int* tokens, int* counts, void* stream);
+/* fmoe_ep_pack: one payload row per (token, rank) at the row pos[rank, token] of `send`.
+ * hidden_states [T, H] FP8, hidden_states_scale [H/128, T]; both hidden_states and send
+ * 16-byte aligned. */
+int fmoe_ep_pack(const void* hidden_states, const float* hidden_states_scale,
+                 const int* topk_idx, const float* topk_w, const int* pos, int64_t num_tokens,
+                 int hidden_size, int top_k, int world, void* send, void* stream);
+/* fmoe_ep_unpack: `rows` received payload rows -> hidden_states [rows, H] FP8,
+ * hidden_states_scale [H/128, rows], topk_idx / topk_w [rows, top_k] (the inputs of
+ * fmoe_forward_routed). recv and hidden_states 16-byte aligned. */
+int fmoe_ep_unpack(const void* recv, int64_t rows, int hidden_size, int top_k,
+                   void* hidden_states, float* hidden_states_scale, int* topk_idx,
+                   float* topk_w, void* stream);
+/* fmoe_ep_combine: output [T, H] bf16 = per token, the bf16 partial rows back[pos[r, t]]
+ * (rows in send order, as returned by the ranks) summed in fp32 in rank order starting from
+ * 0, then rounded to bf16; tokens with no route get zeros. back and output 16-byte aligned. */
+int fmoe_ep_combine(const void* back, const int* pos, int64_t num_tokens, int hidden_size,
+                    int world, void* output, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

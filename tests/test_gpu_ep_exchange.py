@@ -1,0 +1,123 @@
+"""The expert-parallel exchange kernels (fmoe_ep_plan / pack / unpack / combine) on one B200,
+bit for bit against the framework-op restatement in fmoe_b200/ep.py that the gloo CPU tests
+exercise, plus the whole layer with the exchange kernels on and off (world size 1)."""
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parent.parent
+for _p in (ROOT, ROOT / "fused-moe-yws_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+pytestmark = pytest.mark.gpu
+
+
+def _routing(T, K, E, world, seed, drop=0.1):
+    g = torch.Generator().manual_seed(seed)
+    if T == 0:
+        return (torch.empty(0, K, dtype=torch.int32, device="cuda"),
+                torch.empty(0, K, dtype=torch.float32, device="cuda"))
+    idx = torch.stack([torch.randperm(E, generator=g)[:K] for _ in range(T)]).to(torch.int32)
+    idx[torch.rand(T, K, generator=g) < drop] = -1  # unselected slots
+    w = torch.rand(T, K, generator=g)
+    return idx.cuda(), w.cuda()
+
+
+def _torch_plan(idx, world, e_per_rank):
+    T, K = idx.shape
+    owner = torch.where(idx >= 0, idx // e_per_rank, torch.full_like(idx, -1))
+    mask = torch.zeros(T, world, dtype=torch.bool, device=idx.device)
+    valid = owner >= 0
+    rows = torch.arange(T, device=idx.device).unsqueeze(1).expand(T, K)
+    mask[rows[valid], owner[valid].long()] = True
+    order = torch.nonzero(mask.t(), as_tuple=False)
+    return mask.sum(0), order[:, 1], mask
+
+
+@pytest.mark.parametrize("T,world", [(1, 1), (37, 2), (1500, 4), (4096, 8), (0, 2)])
+def test_plan_matches_restatement(T, world):
+    import fmoe_b200
+
+    E, K = 256, 8
+    idx, _ = _routing(T, K, E, world, seed=T + world)
+    pos, tokens, counts = fmoe_b200.ep_plan(idx, world, E // world)
+    cnt_ref, tok_ref, mask = _torch_plan(idx, world, E // world)
+    assert counts.tolist() == cnt_ref.tolist()
+    n = int(cnt_ref.sum())
+    assert torch.equal(tokens[:n].long(), tok_ref)
+    # pos[d, t] is the row of t in d's segment, -1 where t does not go to d
+    base = torch.cumsum(cnt_ref, 0) - cnt_ref
+    for d in range(world):
+        sel = mask[:, d]
+        expect = torch.full((T,), -1, dtype=torch.int64, device=idx.device)
+        expect[sel] = base[d] + torch.arange(int(sel.sum()), device=idx.device)
+        assert torch.equal(pos[d].long(), expect)
+
+
+@pytest.mark.parametrize("H,K,T,world", [(7168, 8, 300, 4), (256, 4, 33, 2)])
+def test_pack_unpack_match_restatement(H, K, T, world):
+    import fmoe_b200
+    from fmoe_b200 import ep
+
+    E = 256 if K == 8 else 16
+    idx, w = _routing(T, K, E, world, seed=H + T)
+    g = torch.Generator().manual_seed(3)
+    hs = (torch.randn(T, H, generator=g) * 4).to(torch.float8_e4m3fn).cuda()
+    sc = torch.rand(H // 128, T, generator=g).cuda()
+    pos, tokens, counts = fmoe_b200.ep_plan(idx, world, E // world)
+    n = int(counts.sum())
+    send = fmoe_b200.ep_pack(hs, sc, idx, w, pos, n)
+    ref = ep.pack_rows(hs, sc, idx, w, tokens[:n].long())
+    assert torch.equal(send, ref)
+    hs_r, sc_r, idx_r, w_r = fmoe_b200.ep_unpack(send, H, K)
+    r_hs, r_sc, r_idx, r_w = ep.unpack_rows(ref, H, K)
+    assert torch.equal(hs_r.view(torch.uint8), r_hs.view(torch.uint8))
+    assert torch.equal(sc_r, r_sc) and torch.equal(idx_r, r_idx) and torch.equal(w_r, r_w)
+
+
+@pytest.mark.parametrize("T,world", [(513, 4), (64, 8), (5, 1)])
+def test_combine_matches_rank_ordered_index_add(T, world):
+    import fmoe_b200
+
+    H, K, E = 7168, 8, 256
+    idx, _ = _routing(T, K, E, world, seed=11 * T)
+    pos, tokens, counts = fmoe_b200.ep_plan(idx, world, E // world)
+    n = int(counts.sum())
+    g = torch.Generator().manual_seed(5)
+    back = (torch.randn(n, H, generator=g) * 3).to(torch.bfloat16).cuda()
+    out = fmoe_b200.ep_combine(back, pos, T)
+    ref = torch.zeros(T, H, dtype=torch.float32, device="cuda")
+    start = 0
+    tok = tokens[:n].long()
+    for c in counts.tolist():
+        if c:
+            ref.index_add_(0, tok[start:start + c], back[start:start + c].float())
+        start += c
+    assert torch.equal(out, ref.to(torch.bfloat16))
+
+
+def test_layer_same_with_and_without_exchange_kernels():
+    from fmoe_b200 import ep
+    from fmoe_b200 import workloads as W
+
+    geo = W.DSV3
+    weights = W.make_expert_slice(geo, 7, 0, 256, device="cuda")
+    acts = W.make_activations(geo, 96, 21, device="cuda")
+    a4 = [acts[k] for k in W.OPERATOR_ARGS[:4]]
+    fused = ep.ExpertParallelMoE(weights=weights, fused_exchange=True).forward(*a4)
+    plain = ep.ExpertParallelMoE(weights=weights, fused_exchange=False).forward(*a4)
+    torch.cuda.synchronize()
+    assert torch.equal(fused, plain)
+
+
+def test_exchange_entry_points_reject_bad_arguments():
+    import fmoe_b200
+
+    lib = fmoe_b200.load_library()
+    assert lib.fmoe_ep_plan(None, 4, 8, 2, 128, None, None, None, None) == fmoe_b200.FMOE_ERR_VALUE
+    assert lib.fmoe_ep_combine(None, None, 4, 7168, 0, None, None) == fmoe_b200.FMOE_ERR_VALUE
+    assert lib.fmoe_ep_unpack(None, 3, 100, 8, None, None, None, None, None) == \
+        fmoe_b200.FMOE_ERR_VALUE
