@@ -56,23 +56,26 @@ __global__ void __launch_bounds__(256) scatter_gather_kernel(ScatterArgs a) {
   const int v0 = (int)((int64_t)vpr * blockIdx.y / gridDim.y);
   const int v1 = (int)((int64_t)vpr * (blockIdx.y + 1) / gridDim.y);
   const int vw = v1 - v0;
-  const int kb = a.H / kBlock;
+  // this CTA also owns the 128-column scale blocks that start inside its columns, so the
+  // scattered 4-byte scale stores are spread over every column part
+  const int kb0 = (v0 * 16 + kBlock - 1) / kBlock, kb1 = (v1 * 16 + kBlock - 1) / kBlock;
+  const int kbw = kb1 - kb0;
   // The source rows and their scales were complete before the routing kernel passed its
   // own dependency wait (this grid starts only after that), so they are fetched before
   // this kernel's wait: the HBM latency of the copy overlaps the routing kernel instead
   // of following it. Only small slices are prefetched (decode-sized batches).
   const bool pre_rows = kTok * vw <= kPreVec;
-  const bool pre_scales = blockIdx.y == 0 && kTok * kb <= kPreScales;
+  const bool pre_scales = kTok * kbw <= kPreScales;
   if (pre_rows) {
     for (int v = tid; v < kTok * vw; v += blockDim.x) {
       const int64_t t = t0 + v / vw;
       if (t < a.T) s_pre[v] = ld_nc_v4(a.hidden + t * a.H + (v0 + v % vw) * 16);
     }
   }
-  if (pre_scales) {
-    for (int v = tid; v < kTok * kb; v += blockDim.x) {
-      const int64_t t = t0 + v / kb;
-      if (t < a.T) s_pscale[v] = __ldg(a.hidden_scale + (int64_t)(v % kb) * a.T + t);
+  if (pre_scales && kbw > 0) {
+    for (int v = tid; v < kTok * kbw; v += blockDim.x) {
+      const int64_t t = t0 + v / kbw;
+      if (t < a.T) s_pscale[v] = __ldg(a.hidden_scale + (int64_t)(kb0 + v % kbw) * a.T + t);
     }
   }
   pdl_wait();
@@ -150,13 +153,14 @@ __global__ void __launch_bounds__(256) scatter_gather_kernel(ScatterArgs a) {
                              : ld_nc_v4(a.hidden + (t0 + tok) * a.H + (v0 + pv) * 16);
     *reinterpret_cast<uint4*>(a.a_perm + (int64_t)s_row[i] * a.H + (v0 + pv) * 16) = x;
   }
-  if (blockIdx.y == 0) {
-    for (int v = tid; v < n * kb; v += blockDim.x) {
-      const int li = v / kb, b = v - li * kb;
+  if (kbw > 0) {
+    for (int v = tid; v < n * kbw; v += blockDim.x) {
+      const int li = v / kbw, bb = v - li * kbw;
       const int i = s_list[li];
       const int tok = i / K;
-      a.a_scale[(int64_t)b * a.row_cap + s_row[i]] =
-          pre_scales ? s_pscale[tok * kb + b] : a.hidden_scale[(int64_t)b * a.T + t0 + tok];
+      a.a_scale[(int64_t)(kb0 + bb) * a.row_cap + s_row[i]] =
+          pre_scales ? s_pscale[tok * kbw + bb]
+                     : a.hidden_scale[(int64_t)(kb0 + bb) * a.T + t0 + tok];
     }
   }
   // padding rows of the experts this CTA column owns (expert e goes to x = e % gridDim.x)
@@ -171,11 +175,11 @@ __global__ void __launch_bounds__(256) scatter_gather_kernel(ScatterArgs a) {
       if (r < a.row_cap)
         *reinterpret_cast<uint4*>(a.a_perm + (int64_t)r * a.H + (v0 + v % vw) * 16) = z;
     }
+    for (int v = tid; v < npad * kbw; v += blockDim.x) {
+      const int r = r0 + v / kbw;
+      if (r < a.row_cap) a.a_scale[(int64_t)(kb0 + v % kbw) * a.row_cap + r] = 0.0f;
+    }
     if (blockIdx.y == 0) {
-      for (int v = tid; v < npad * kb; v += blockDim.x) {
-        const int r = r0 + v / kb;
-        if (r < a.row_cap) a.a_scale[(int64_t)(v % kb) * a.row_cap + r] = 0.0f;
-      }
       for (int v = tid; v < npad; v += blockDim.x) {
         if (r0 + v < a.row_cap) {
           a.row_token[r0 + v] = -1;
