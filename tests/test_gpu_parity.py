@@ -177,9 +177,9 @@ def test_forward_tiny_throughput_family(fmoe, oracle_mod, T, geo, offset):
     assert _device_error(fmoe, geo, T, offset, tile_n=128) == 0
 
 
-def test_plan_bitexact(fmoe, oracle_mod):
+@pytest.mark.parametrize("T", [777, 64, 17, 1])
+def test_plan_bitexact(fmoe, oracle_mod, T):
     geo = W.DSV3
-    T = 777
     gpu, cpu, _ = _inputs(geo, T, seed=4)
     _run(fmoe, geo, gpu, 0, 2.5)
     prob = fmoe.make_problem(T, geo.num_experts, geo.num_local, geo.hidden, geo.inter, 0, 2.5)
@@ -193,6 +193,23 @@ def test_plan_bitexact(fmoe, oracle_mod):
     assert np.array_equal(view["row_token"].cpu().numpy()[:total], plan["row_token"][:total])
     assert np.array_equal(view["token_row"].cpu().numpy(), plan["token_row"].ravel())
     assert int(view["meta"][1]) == total
+
+
+@pytest.mark.parametrize("T", [1, 5, 64, 300])
+def test_operator_equals_route_then_routed_entry_point(fmoe, T):
+    """fmoe_forward == fmoe_route followed by fmoe_forward_routed on the same routing
+    (the expert-parallel layer's local step), bit for bit."""
+    geo = W.DSV3
+    gpu, _, _ = _inputs(geo, T, seed=9)
+    out = _run(fmoe, geo, gpu, 0, 2.5)
+    idx, w = fmoe.route(gpu["routing_logits"], gpu["routing_bias"], 8, 4, 8, 2.5,
+                        num_local_experts=geo.num_local)
+    routed = fmoe.forward_routed(idx, w, gpu["hidden_states"], gpu["hidden_states_scale"],
+                                 gpu["gemm1_weights"], gpu["gemm1_weights_scale"],
+                                 gpu["gemm2_weights"], gpu["gemm2_weights_scale"], 0,
+                                 geo.num_experts, n_group=8, topk_group=4)
+    torch.cuda.synchronize()
+    assert torch.equal(out, routed)
 
 
 def test_deterministic_and_rsf_scaling(fmoe):
