@@ -349,7 +349,7 @@ def run_ep(args, world, rank, local):
     per = 256 // world
     weights = W.make_expert_slice(geo, args.seed, rank * per, per, device="cuda")
     acts = W.make_activations(geo, T, args.seed + 1009 * rank, device="cuda")
-    layer = ep.ExpertParallelMoE(weights=weights)
+    layer = ep.ExpertParallelMoE(weights=weights, exchange=args.exchange)
     a4 = [acts[k] for k in W.OPERATOR_ARGS[:4]]
     for _ in range(args.warmup):
         layer.forward(*a4)
@@ -410,7 +410,10 @@ def run_ep(args, world, rank, local):
         "config": {"workload": "config3_dsv3_ep", "tokens_per_rank": T, "hidden": 7168,
                    "intermediate": 2048, "experts": 256, "experts_per_rank": per, "top_k": 8,
                    "n_group": 8, "topk_group": 4, "parallelism": f"ep{world}",
-                   "collectives": "NCCL all-to-all-v dispatch + combine, counts all-to-all",
+                   "collectives": ("rows stored into the peers' buffers over NVLink (CUDA IPC), "
+                                   "counts all-gather and one-element all-reduce barriers (NCCL)"
+                                   if args.exchange == "p2p" else
+                                   "NCCL all-to-all-v dispatch + combine, counts all-to-all"),
                    "l2": f"weights {per * 44.05 / 1000:.1f} GB per rank > L2"},
         "breakdown_ms_max_over_ranks": {"route": round(float(br[0]), 3),
                                         "dispatch": round(float(br[1]), 3),
@@ -419,8 +422,10 @@ def run_ep(args, world, rank, local):
         "clocks": clk.summary(),
         "e2e": {"value": round(world * T / (e2e_ms * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": T * geo.hidden * 2},
-        "gpu_launches": (1 + 5) * args.steps,
+        # routing, send plan, pack, unpack, the operator's 5 kernels, (P2P: return), combine
+        "gpu_launches": (10 + (args.exchange == "p2p")) * args.steps,
     }
+    layer.close()
     return line
 
 
@@ -502,6 +507,8 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p",
+                    help="expert-parallel runs (N > 1): rows over peer memory or NCCL all-to-all")
     ap.add_argument("--sweep-tiles", default="0",
                     help="comma-separated token tiles timed per sweep case (0 = autotune)")
     args = ap.parse_args()

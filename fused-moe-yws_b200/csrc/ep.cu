@@ -19,6 +19,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <cstring>
 #include <string>
 
 #include "fmoe.h"
@@ -200,6 +201,67 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const __nv_bfloat16* ba
   }
 }
 
+
+// P2P dispatch: the payload row of (token t, rank d) goes straight into rank d's receive
+// buffer at row pos[d, t] + shift[d] (peer memory over NVLink; plain stores, no multicast).
+// Rows outside [0, capacity) are dropped and flagged. A system fence makes the rows visible
+// to the peers once the kernel has completed.
+__global__ void __launch_bounds__(256) ep_pack_p2p_kernel(
+    const uint8_t* hidden, const float* hscale, const int* idx, const float* w, const int* pos,
+    int64_t T, int H, int K, int world, uint8_t* const* peer_recv, const int64_t* shift,
+    int64_t capacity, int* err) {
+  const int64_t t = blockIdx.x;
+  const int kb = H / kBlock;
+  const int64_t row_bytes = (int64_t)H + 4 * kb + 8 * K;
+  for (int d = 0; d < world; ++d) {
+    const int r0 = pos[(int64_t)d * T + t];
+    if (r0 < 0) continue;
+    const int64_t r = r0 + shift[d];
+    if (r < 0 || r >= capacity) {
+      if (threadIdx.x == 0) atomicOr(err, 1);
+      continue;
+    }
+    uint8_t* dst = peer_recv[d] + r * row_bytes;
+    if (row_bytes % 16 == 0) {
+      for (int v = threadIdx.x; v < H / 16; v += blockDim.x)
+        reinterpret_cast<uint4*>(dst)[v] =
+            __ldg(reinterpret_cast<const uint4*>(hidden + t * H) + v);
+    } else {
+      for (int v = threadIdx.x; v < H / 4; v += blockDim.x)
+        reinterpret_cast<uint32_t*>(dst)[v] =
+            __ldg(reinterpret_cast<const uint32_t*>(hidden + t * H) + v);
+    }
+    float* ds = reinterpret_cast<float*>(dst + H);
+    for (int b = threadIdx.x; b < kb; b += blockDim.x) ds[b] = __ldg(hscale + (int64_t)b * T + t);
+    int* di = reinterpret_cast<int*>(dst + H + 4 * kb);
+    float* dw = reinterpret_cast<float*>(dst + H + 4 * kb + 4 * K);
+    for (int k = threadIdx.x; k < K; k += blockDim.x) {
+      di[k] = __ldg(idx + t * K + k);
+      dw[k] = __ldg(w + t * K + k);
+    }
+  }
+  __threadfence_system();
+}
+
+// P2P return: received row r (from source rank s, rows [src_start[s], src_start[s + 1]))
+// goes back into rank s's buffer at row r + shift[s], as bf16 [H].
+__global__ void __launch_bounds__(256) ep_return_p2p_kernel(
+    const __nv_bfloat16* part, int64_t R, int H, int world, const int64_t* src_start,
+    __nv_bfloat16* const* peer_back, const int64_t* shift, int64_t capacity, int* err) {
+  const int64_t r = blockIdx.x;
+  int s = 0;
+  while (s + 1 < world && r >= src_start[s + 1]) ++s;
+  const int64_t q = r + shift[s];
+  if (q < 0 || q >= capacity) {
+    if (threadIdx.x == 0) atomicOr(err, 2);
+    return;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(part + r * H);
+  uint4* dst = reinterpret_cast<uint4*>(peer_back[s] + q * H);
+  for (int v = threadIdx.x; v < H / 8; v += blockDim.x) dst[v] = __ldg(src + v);
+  __threadfence_system();
+}
+
 int ep_fail(int code, const std::string& msg) {
   set_last_error(msg);
   return code;
@@ -285,4 +347,74 @@ extern "C" int fmoe_ep_combine(const void* back, const int* pos, int64_t num_tok
       static_cast<const __nv_bfloat16*>(back), pos, num_tokens, hidden_size, world,
       static_cast<__nv_bfloat16*>(output));
   return ep_check_launch("fmoe_ep_combine");
+}
+
+// ---- peer buffers (CUDA IPC) and the P2P exchange ------------------------------------------
+extern "C" int fmoe_ep_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_ipc_alloc: bad arguments");
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess) return ep_fail(FMOE_ERR_RUNTIME, cudaGetErrorString(e));
+  e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), *ptr);
+  if (e != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return ep_fail(FMOE_ERR_RUNTIME, cudaGetErrorString(e));
+  }
+  return FMOE_OK;
+}
+
+extern "C" int fmoe_ep_ipc_open(const void* handle, void** ptr) {
+  if (!ptr || !handle) return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_ipc_open: bad arguments");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return ep_fail(FMOE_ERR_RUNTIME, cudaGetErrorString(e));
+  return FMOE_OK;
+}
+
+extern "C" int fmoe_ep_ipc_close(void* ptr) {
+  const cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? FMOE_OK : ep_fail(FMOE_ERR_RUNTIME, cudaGetErrorString(e));
+}
+
+extern "C" int fmoe_ep_ipc_free(void* ptr) {
+  const cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? FMOE_OK : ep_fail(FMOE_ERR_RUNTIME, cudaGetErrorString(e));
+}
+
+extern "C" int fmoe_ep_pack_p2p(const void* hidden_states, const float* hidden_states_scale,
+                                const int* topk_idx, const float* topk_w, const int* pos,
+                                int64_t num_tokens, int hidden_size, int top_k, int world,
+                                void* const* peer_recv, const int64_t* row_shift,
+                                int64_t capacity_rows, int* err, void* stream) {
+  if (!ep_geometry_ok(num_tokens, hidden_size, top_k, world))
+    return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_pack_p2p: bad geometry");
+  if (num_tokens == 0) return FMOE_OK;
+  if (!hidden_states || !hidden_states_scale || !topk_idx || !topk_w || !pos || !peer_recv ||
+      !row_shift || !err)
+    return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_pack_p2p: NULL pointer");
+  if (reinterpret_cast<uintptr_t>(hidden_states) % 16)
+    return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_pack_p2p: hidden_states must be 16-byte aligned");
+  ep_pack_p2p_kernel<<<(unsigned)num_tokens, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(hidden_states), hidden_states_scale, topk_idx, topk_w, pos,
+      num_tokens, hidden_size, top_k, world, reinterpret_cast<uint8_t* const*>(peer_recv),
+      row_shift, capacity_rows, err);
+  return ep_check_launch("fmoe_ep_pack_p2p");
+}
+
+extern "C" int fmoe_ep_return_p2p(const void* partial, int64_t rows, int hidden_size, int world,
+                                  const int64_t* src_start, void* const* peer_back,
+                                  const int64_t* row_shift, int64_t capacity_rows, int* err,
+                                  void* stream) {
+  if (!ep_geometry_ok(rows, hidden_size, 1, world))
+    return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_return_p2p: bad geometry");
+  if (rows == 0) return FMOE_OK;
+  if (!partial || !src_start || !peer_back || !row_shift || !err)
+    return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_return_p2p: NULL pointer");
+  if (reinterpret_cast<uintptr_t>(partial) % 16)
+    return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_return_p2p: partial must be 16-byte aligned");
+  ep_return_p2p_kernel<<<(unsigned)rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(partial), rows, hidden_size, world, src_start,
+      reinterpret_cast<__nv_bfloat16* const*>(peer_back), row_shift, capacity_rows, err);
+  return ep_check_launch("fmoe_ep_return_p2p");
 }

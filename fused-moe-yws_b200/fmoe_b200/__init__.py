@@ -33,7 +33,9 @@ EXPORTED_SYMBOLS = ("fmoe_abi_version", "fmoe_last_error", "fmoe_validate", "fmo
                     "fmoe_autotune_tile_n", "fmoe_forward", "fmoe_route", "fmoe_read_device_error",
                     "fmoe_plan_view_get", "fmoe_set_stage_events", "fmoe_route_static",
                     "fmoe_forward_routed", "fmoe_selftest_wait_timeout", "fmoe_ep_plan",
-                    "fmoe_ep_pack", "fmoe_ep_unpack", "fmoe_ep_combine")
+                    "fmoe_ep_pack", "fmoe_ep_unpack", "fmoe_ep_combine", "fmoe_ep_ipc_alloc",
+                    "fmoe_ep_ipc_open", "fmoe_ep_ipc_close", "fmoe_ep_ipc_free",
+                    "fmoe_ep_pack_p2p", "fmoe_ep_return_p2p")
 
 
 class FmoeProblem(ctypes.Structure):
@@ -103,6 +105,13 @@ def load_library(path: Path | str | None = None):
         lib.fmoe_ep_pack.argtypes = [vp, vp, vp, vp, vp, i64, i32, i32, i32, vp, vp]
         lib.fmoe_ep_unpack.argtypes = [vp, i64, i32, i32, vp, vp, vp, vp, vp]
         lib.fmoe_ep_combine.argtypes = [vp, vp, i64, i32, i32, vp, vp]
+        lib.fmoe_ep_ipc_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp), vp]
+        lib.fmoe_ep_ipc_open.argtypes = [vp, ctypes.POINTER(vp)]
+        lib.fmoe_ep_ipc_close.argtypes = [vp]
+        lib.fmoe_ep_ipc_free.argtypes = [vp]
+        lib.fmoe_ep_pack_p2p.argtypes = [vp, vp, vp, vp, vp, i64, i32, i32, i32, vp, vp, i64, vp,
+                                         vp]
+        lib.fmoe_ep_return_p2p.argtypes = [vp, i64, i32, i32, vp, vp, vp, i64, vp, vp]
         for name in EXPORTED_SYMBOLS:
             if not hasattr(lib, name):
                 raise RuntimeError(f"{p} does not export {name}")
@@ -365,33 +374,123 @@ def ep_pack(hidden_states, hidden_states_scale, topk_idx, topk_w, pos, rows: int
     return send
 
 
-def ep_unpack(recv: torch.Tensor, H: int, K: int):
-    """Received rows -> (hidden fp8 [R, H], scale fp32 [H/128, R], idx int32, w fp32)."""
-    R = recv.shape[0]
-    dev = recv.device
+def ep_unpack(recv, H: int, K: int, rows: int = None, device=None):
+    """Received rows -> (hidden fp8 [R, H], scale fp32 [H/128, R], idx int32, w fp32).
+    `recv` is a uint8 tensor of payload rows, or a raw device pointer (int) with `rows` and
+    `device` given."""
+    if isinstance(recv, int):
+        R, dev, ptr = rows, device, recv
+    else:
+        R, dev, ptr = recv.shape[0], recv.device, recv.data_ptr()
     lib = load_library()
     hs = torch.empty(R, H, dtype=torch.float8_e4m3fn, device=dev)
     sc = torch.empty(H // 128, R, dtype=torch.float32, device=dev)
     idx = torch.empty(R, K, dtype=torch.int32, device=dev)
     w = torch.empty(R, K, dtype=torch.float32, device=dev)
-    rc = lib.fmoe_ep_unpack(recv.data_ptr(), R, H, K, hs.data_ptr(), sc.data_ptr(),
+    rc = lib.fmoe_ep_unpack(ptr, R, H, K, hs.data_ptr(), sc.data_ptr(),
                             idx.data_ptr(), w.data_ptr(), _stream(dev))
     if rc != FMOE_OK:
         _raise(lib, rc, "ep_unpack")
     return hs, sc, idx, w
 
 
-def ep_combine(back: torch.Tensor, pos: torch.Tensor, T: int):
-    """Per token, its returned partial rows summed in fp32 in rank order -> bf16 [T, H]."""
-    H = back.shape[1]
-    dev = back.device
+def ep_combine(back, pos: torch.Tensor, T: int, H: int = None):
+    """Per token, its returned partial rows summed in fp32 in rank order -> bf16 [T, H].
+    `back` is a bf16 tensor [rows, H] or a raw device pointer (int) with `H` given."""
+    if isinstance(back, int):
+        ptr = back
+    else:
+        H, ptr = back.shape[1], back.data_ptr()
+    dev = pos.device
     lib = load_library()
     out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
-    rc = lib.fmoe_ep_combine(back.data_ptr(), pos.data_ptr(), T, H, pos.shape[0],
+    rc = lib.fmoe_ep_combine(ptr, pos.data_ptr(), T, H, pos.shape[0],
                              out.data_ptr(), _stream(dev))
     if rc != FMOE_OK:
         _raise(lib, rc, "ep_combine")
     return out
+
+
+class PeerBuffers:
+    """This rank's receive and return buffers and every peer's, mapped by CUDA IPC.
+
+    Collective: every rank of `group` constructs it with the same sizes (the handles are
+    exchanged with all_gather_object). `recv[r]` / `back[r]` hold rank r's buffers as device
+    addresses in this process; `recv_ptrs` / `back_ptrs` are the same as device int64 arrays
+    for the P2P kernels."""
+
+    def __init__(self, recv_bytes: int, back_bytes: int, group, device):
+        import torch.distributed as dist
+
+        lib = load_library()
+        self._lib = lib
+        self.recv_bytes, self.back_bytes = recv_bytes, back_bytes
+        rank, world = dist.get_rank(group), dist.get_world_size(group)
+        own = []
+        handles = []
+        with torch.cuda.device(device):
+            for nbytes in (recv_bytes, back_bytes):
+                ptr = ctypes.c_void_p()
+                h = ctypes.create_string_buffer(64)
+                rc = lib.fmoe_ep_ipc_alloc(nbytes, ctypes.byref(ptr), h)
+                if rc != FMOE_OK:
+                    _raise(lib, rc, "ep_ipc_alloc")
+                own.append(ptr.value)
+                handles.append(h.raw)
+            gathered = [None] * world
+            dist.all_gather_object(gathered, handles, group=group)
+            self._opened = []
+            maps = [[0] * world, [0] * world]
+            for r in range(world):
+                for which in range(2):
+                    if r == rank:
+                        maps[which][r] = own[which]
+                        continue
+                    ptr = ctypes.c_void_p()
+                    rc = lib.fmoe_ep_ipc_open(gathered[r][which], ctypes.byref(ptr))
+                    if rc != FMOE_OK:
+                        _raise(lib, rc, "ep_ipc_open")
+                    maps[which][r] = ptr.value
+                    self._opened.append(ptr.value)
+        self._own = own
+        self.recv, self.back = maps
+        self.recv_ptrs = torch.tensor(self.recv, dtype=torch.int64, device=device)
+        self.back_ptrs = torch.tensor(self.back, dtype=torch.int64, device=device)
+
+    def close(self):
+        """Unmap the peers' buffers and free this rank's (after a barrier: no peer may still
+        write into them)."""
+        for ptr in self._opened:
+            self._lib.fmoe_ep_ipc_close(ptr)
+        for ptr in self._own:
+            self._lib.fmoe_ep_ipc_free(ptr)
+        self._opened, self._own = [], []
+
+
+def ep_pack_p2p(hidden_states, hidden_states_scale, topk_idx, topk_w, pos, peers: PeerBuffers,
+                row_shift: torch.Tensor, capacity_rows: int, err: torch.Tensor):
+    T, H = hidden_states.shape
+    K = topk_idx.shape[1]
+    dev = hidden_states.device
+    lib = load_library()
+    rc = lib.fmoe_ep_pack_p2p(hidden_states.data_ptr(), hidden_states_scale.data_ptr(),
+                              topk_idx.data_ptr(), topk_w.data_ptr(), pos.data_ptr(), T, H, K,
+                              pos.shape[0], peers.recv_ptrs.data_ptr(), row_shift.data_ptr(),
+                              capacity_rows, err.data_ptr(), _stream(dev))
+    if rc != FMOE_OK:
+        _raise(lib, rc, "ep_pack_p2p")
+
+
+def ep_return_p2p(partial: torch.Tensor, src_start: torch.Tensor, peers: PeerBuffers,
+                  row_shift: torch.Tensor, capacity_rows: int, err: torch.Tensor):
+    R, H = partial.shape
+    dev = partial.device
+    lib = load_library()
+    rc = lib.fmoe_ep_return_p2p(partial.data_ptr(), R, H, row_shift.shape[0],
+                                src_start.data_ptr(), peers.back_ptrs.data_ptr(),
+                                row_shift.data_ptr(), capacity_rows, err.data_ptr(), _stream(dev))
+    if rc != FMOE_OK:
+        _raise(lib, rc, "ep_return_p2p")
 
 
 def read_device_error(prob: FmoeProblem, workspace: torch.Tensor) -> int:

@@ -21,9 +21,15 @@ combine are all deterministic.
 
 On CUDA the send plan, the payload packing and unpacking and the rank-ordered combine are
 kernels of the library (`fmoe_ep_*` in include/fmoe.h: one launch each, instead of chains
-of framework ops); only the counts cross to the host, because NCCL's all-to-all-v takes
-its split sizes there. The framework-op version below is the CPU restatement the gloo
-tests exercise, and `fused_exchange=False` selects it on CUDA too.
+of framework ops). With more than one rank the rows move over peer memory by default
+(`exchange="p2p"`): every rank's receive and return buffers are mapped into the other
+ranks by CUDA IPC, the pack kernel stores each payload row straight into its destination's
+receive buffer over NVLink, and a return kernel stores each partial output row straight
+into its source's return buffer; a one-element all-reduce on the stream orders the ranks
+after each of the two kernels. Only the per-destination counts (and the token counts, for
+sizing) are gathered to the host. `exchange="nccl"` moves the same rows with NCCL
+all-to-all-v instead. The framework-op version below is the CPU restatement the gloo tests
+exercise, and `fused_exchange=False` selects it on CUDA too.
 """
 from __future__ import annotations
 
@@ -76,7 +82,8 @@ class ExpertParallelMoE:
     def __init__(self, num_experts: int = 256, n_group: int = 8, topk_group: int = 4,
                  top_k: int = 8, routed_scaling_factor: float = 2.5, group=None,
                  weights: Optional[dict] = None, route_fn: Optional[RouteFn] = None,
-                 local_fn: Optional[LocalFn] = None, fused_exchange: bool = True):
+                 local_fn: Optional[LocalFn] = None, fused_exchange: bool = True,
+                 exchange: str = "p2p"):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -92,6 +99,13 @@ class ExpertParallelMoE:
         self.local_fn = local_fn or self._local_gpu
         self.timings = EPTimings()
         self.fused_exchange = fused_exchange
+        if exchange not in ("p2p", "nccl"):
+            raise ValueError(f"exchange must be 'p2p' or 'nccl', not {exchange!r}")
+        self.exchange = exchange
+        self._peers = None       # fmoe_b200.PeerBuffers, sized for _cap_tokens per rank
+        self._cap_tokens = 0
+        self._flag = None
+        self._err = None
 
     # ---- default B200 implementations --------------------------------------------------
     def _route_gpu(self, logits, bias):
@@ -109,6 +123,89 @@ class ExpertParallelMoE:
                                         ws["gemm1_weights_scale"], ws["gemm2_weights"],
                                         ws["gemm2_weights_scale"], offset, self.num_experts,
                                         n_group=self.n_group, topk_group=self.topk_group)
+
+    # ---- peer-memory exchange -----------------------------------------------------------
+    def _barrier(self):
+        # stream-ordered: the next kernels of every rank wait for every rank's previous ones
+        dist.all_reduce(self._flag, group=self.group)
+
+    def _ensure_peers(self, t_max: int, H: int, K: int, dev):
+        """(Re)allocate the IPC-shared buffers for t_max tokens per rank. Every rank calls
+        this with the same t_max (gathered), so the collective steps match."""
+        import fmoe_b200
+
+        if self._peers is not None and t_max <= self._cap_tokens:
+            return
+        if self._peers is not None:
+            self._barrier()
+            torch.cuda.synchronize(dev)
+            self._peers.close()
+        cap = max(64, 1 << (max(t_max, 1) - 1).bit_length())
+        rows = cap * self.world  # a token goes to each rank at most once
+        self._peers = fmoe_b200.PeerBuffers(rows * fmoe_b200.ep_payload_bytes(H, K),
+                                            rows * H * 2, self.group, dev)
+        self._cap_tokens = cap
+        if self._flag is None:
+            self._flag = torch.zeros(1, dtype=torch.int32, device=dev)
+            self._err = torch.zeros(1, dtype=torch.int32, device=dev)
+
+    def exchange_error(self) -> int:
+        """Bits set by the P2P kernels since the last forward (0 = every row in bounds)."""
+        return int(self._err.item()) if self._err is not None else 0
+
+    def close(self):
+        if self._peers is not None:
+            self._barrier()
+            torch.cuda.synchronize()
+            self._peers.close()
+            self._peers = None
+
+    def _forward_p2p(self, idx, w, hidden_states, hidden_states_scale, mark):
+        import fmoe_b200
+
+        T, H = hidden_states.shape
+        K, world, me = self.top_k, self.world, self.rank
+        dev = hidden_states.device
+        pos, _, counts = fmoe_b200.ep_plan(idx, world, self.e_per_rank)
+        meta = torch.cat([counts.to(torch.int64),
+                          torch.tensor([T], dtype=torch.int64, device=dev)])
+        allm = torch.empty(world, world + 1, dtype=torch.int64, device=dev)
+        dist.all_gather_into_tensor(allm, meta, group=self.group)
+        m = allm.tolist()
+        cnt = [row[:world] for row in m]  # cnt[s][d]: rows rank s sends to rank d
+        self._ensure_peers(max(row[world] for row in m), H, K, dev)
+        cap = self._cap_tokens * world
+
+        def src_start(d, s):  # first row of source s in rank d's receive buffer
+            return sum(cnt[q][d] for q in range(s))
+
+        def seg_base(s, d):  # first row of destination d in rank s's send order
+            return sum(cnt[s][:d])
+
+        shift_pack = [src_start(d, me) - seg_base(me, d) for d in range(world)]
+        starts = [src_start(me, s) for s in range(world + 1)]
+        shift_ret = [seg_base(s, me) - starts[s] for s in range(world)]
+        R = starts[world]
+        # the three offset tables in one pinned, asynchronous upload
+        host = torch.tensor(shift_pack + starts + shift_ret, dtype=torch.int64).pin_memory()
+        tables = torch.empty(host.numel(), dtype=torch.int64, device=dev)
+        tables.copy_(host, non_blocking=True)
+        shift_pack_t = tables[:world]
+        starts_t = tables[world:2 * world + 1]
+        shift_ret_t = tables[2 * world + 1:]
+        self._err.zero_()
+        fmoe_b200.ep_pack_p2p(hidden_states, hidden_states_scale, idx, w, pos, self._peers,
+                              shift_pack_t, cap, self._err)
+        self._barrier()
+        hs_r, sc_r, idx_r, w_r = fmoe_b200.ep_unpack(self._peers.recv[me], H, K, rows=R,
+                                                     device=dev)
+        mark()
+        part = self.local_fn(idx_r, w_r, hs_r, sc_r, self.local_offset)
+        mark()
+        fmoe_b200.ep_return_p2p(part.contiguous(), starts_t, self._peers, shift_ret_t, cap,
+                                self._err)
+        self._barrier()
+        return fmoe_b200.ep_combine(self._peers.back[me], pos, T, H)
 
     # ---- the layer -------------------------------------------------------------------------
     def forward(self, routing_logits, routing_bias, hidden_states, hidden_states_scale,
@@ -130,6 +227,14 @@ class ExpertParallelMoE:
         w = w.to(torch.float32).contiguous()
         mark()
         fused = self.fused_exchange and dev.type == "cuda"
+        if fused and self.world > 1 and self.exchange == "p2p":
+            res = self._forward_p2p(idx, w, hidden_states, hidden_states_scale, mark)
+            mark()
+            if timed and len(ev) == 5:
+                torch.cuda.synchronize()
+                self.timings = EPTimings(ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2]),
+                                         ev[2].elapsed_time(ev[3]), ev[3].elapsed_time(ev[4]))
+            return res
         if fused:
             import fmoe_b200
 

@@ -198,6 +198,32 @@ int fmoe_ep_unpack(const void* recv, int64_t rows, int hidden_size, int top_k,
 int fmoe_ep_combine(const void* back, const int* pos, int64_t num_tokens, int hidden_size,
                     int world, void* output, void* stream);
 
+/* Exchange over peer memory instead of a collective library: each rank's receive buffer
+ * and return buffer are device allocations shared with the other ranks by CUDA IPC
+ * (fmoe_ep_ipc_alloc returns the 64-byte cudaIpcMemHandle_t, fmoe_ep_ipc_open maps a peer's
+ * buffer into this process). The P2P kernels write with plain stores over NVLink (no
+ * multicast) and end with a system-scope fence; the caller orders the ranks with a barrier
+ * after each of them (e.g. a one-element all-reduce on the stream).
+ *
+ * fmoe_ep_pack_p2p: the payload row of (token t, rank d) goes to peer_recv[d] at row
+ *   pos[d, t] + row_shift[d]; peer_recv and row_shift are device arrays of world entries.
+ * fmoe_ep_return_p2p: received row r, from the source rank s with
+ *   src_start[s] <= r < src_start[s + 1] (device array of world + 1), goes to peer_back[s] at
+ *   row r + row_shift[s], as H bf16.
+ * Rows outside [0, capacity_rows) are not written; they set bit 0 (pack) or 1 (return) of *err
+ * (a device int the caller clears and reads). */
+int fmoe_ep_ipc_alloc(size_t bytes, void** ptr, void* handle);
+int fmoe_ep_ipc_open(const void* handle, void** ptr);
+int fmoe_ep_ipc_close(void* ptr);
+int fmoe_ep_ipc_free(void* ptr);
+int fmoe_ep_pack_p2p(const void* hidden_states, const float* hidden_states_scale,
+                     const int* topk_idx, const float* topk_w, const int* pos, int64_t num_tokens,
+                     int hidden_size, int top_k, int world, void* const* peer_recv,
+                     const int64_t* row_shift, int64_t capacity_rows, int* err, void* stream);
+int fmoe_ep_return_p2p(const void* partial, int64_t rows, int hidden_size, int world,
+                       const int64_t* src_start, void* const* peer_back, const int64_t* row_shift,
+                       int64_t capacity_rows, int* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -57,9 +57,15 @@ def _worker(rank, world, port, T, q):
     full = W.make_expert_slice(geo, 7, 0, 256, device="cuda")
     local = {k: v[rank * per:(rank + 1) * per].contiguous() for k, v in full.items()}
     acts = W.make_activations(geo, T, 500 + rank, device="cuda")
-    layer = ep.ExpertParallelMoE(weights=local)
-    out = layer.forward(acts["routing_logits"], acts["routing_bias"], acts["hidden_states"],
-                        acts["hidden_states_scale"])
+    layer = ep.ExpertParallelMoE(weights=local)  # rows over peer memory (CUDA IPC, NVLink)
+    a4 = [acts["routing_logits"], acts["routing_bias"], acts["hidden_states"],
+          acts["hidden_states_scale"]]
+    out = layer.forward(*a4)
+    again = layer.forward(*a4)  # buffers reused across calls
+    p2p_err = layer.exchange_error()
+    via_nccl = ep.ExpertParallelMoE(weights=local, exchange="nccl").forward(*a4)
+    layer.close()
+    same_rows = bool(torch.equal(out, via_nccl)) and bool(torch.equal(out, again))
     args = [acts[k] for k in W.OPERATOR_ARGS[:4]] + [full[k] for k in W.OPERATOR_ARGS[4:]]
     ref = fmoe_b200.kernel(*args, 0, 2.5)
     slices = torch.zeros(T, geo.hidden, dtype=torch.float32, device="cuda")
@@ -68,7 +74,7 @@ def _worker(rank, world, port, T, q):
         a = [acts[k] for k in W.OPERATOR_ARGS[:4]] + [sl[k] for k in W.OPERATOR_ARGS[4:]]
         slices += fmoe_b200.kernel(*a, 32 * s, 2.5).float()
     torch.cuda.synchronize()
-    q.put((rank, _close(out, ref), _close(ref, slices)))
+    q.put((rank, _close(out, ref), _close(ref, slices), same_rows, p2p_err))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -85,6 +91,8 @@ def test_ep_two_gpus_matches_full_layer():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for rank, (ok_ep, rel_ep), (ok_sl, rel_sl) in res:
+    for rank, (ok_ep, rel_ep), (ok_sl, rel_sl), same_rows, p2p_err in res:
         assert ok_ep and rel_ep < 1e-2, (rank, rel_ep)
         assert ok_sl and rel_sl < 1e-2, (rank, rel_sl)
+        assert same_rows, rank  # peer-memory and NCCL exchanges give identical outputs
+        assert p2p_err == 0, (rank, p2p_err)
