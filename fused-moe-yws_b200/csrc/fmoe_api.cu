@@ -363,6 +363,7 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   GemmArgs g;
   g.chunks = c.at<Chunk>(c.L.chunks);
   g.meta = c.at<int>(c.L.meta);
+  g.expert_cnt = c.at<int>(c.L.expert_cnt);
   g.H = H;
   g.I = I;
   g.row_cap = c.L.row_cap;

@@ -55,6 +55,7 @@ struct ScatterArgs {
 struct GemmArgs {
   const Chunk* chunks;
   const int* meta;
+  const int* expert_cnt;   // routed rows per local expert
   int m_tiles;             // weight-row tiles per expert (I/128 for GEMM1, H/128 for GEMM2)
   int k_steps;             // 128-wide K steps: H/128 (GEMM1) or I/128 (GEMM2)
   int H, I;

@@ -203,7 +203,13 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     // ------------------------------------------------------------------ TMA producer
     // The whole warp stages each tile's weight block scales into a 2-slot shared ring;
     // lane 0 alone issues the copies.
-    const uint64_t pol_w = policy_evict_first();
+    // Weight tiles: every token tile of an expert reads the same weight rows. The data-parallel
+    // prefix deals tiles round-robin, so one wave of CTAs covers gridDim.x consecutive tiles;
+    // when an expert's tiles fit in one wave its weight rows are read close together in time
+    // and are not worth keeping, when they span several waves the later waves re-read them
+    // from L2 only if they were kept.
+    const uint64_t pol_once = policy_evict_first();
+    const uint64_t pol_keep = policy_evict_last();
     const uint64_t pol_a = policy_evict_last();
     int it = 0, wseg = 0;
     bool ok = true;
@@ -212,6 +218,8 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     while (ok && sched.next(tile, k0, k1)) {
       const Chunk ch = args.chunks[tile / args.m_tiles];
       const int m = tile % args.m_tiles;
+      const int e_tiles = (__ldg(args.expert_cnt + ch.expert) + 127) / 128 * args.m_tiles;
+      const uint64_t pol_w = e_tiles > (int)gridDim.x ? pol_keep : pol_once;
       {
         // GEMM1: gate block m and up block I/128 + m (H/128 values each);
         // GEMM2: h blocks 2 m and 2 m + 1 (I/128 values each)
