@@ -54,6 +54,7 @@ FLOP_PER_ROW = 88_080_384          # 2*H*2I + 2*I*H for DS-V3
 BYTES_PER_EXPERT = 44_050_944      # W13 + W2 FP8 + their fp32 block scales
 GEMM1_BYTES_PER_EXPERT = 29_360_128 + 32 * 56 * 4
 GEMM1_BYTES_PER_ROW = 7168 + 56 * 4 + 2 * 2048 + 16 * 4
+GEMM1_FLOP_PER_ROW = 2 * 7168 * 2 * 2048
 L2_FLUSH_BYTES = 256 << 20
 
 
@@ -287,13 +288,13 @@ def time_e2e(inp, steps, warmup):
     return res[0], res[1], h2d, d2h
 
 
-def cpu_baseline(T, seed):
+def cpu_baseline(T, seed, skew=0):
     """CPU oracle on this host's cores, one call of the same workload (bounded sample)."""
     import oracle
 
     torch.set_num_threads(os.cpu_count() or 1)
     geo = W.DSV3
-    inp = make_workload(T, seed, device="cpu")
+    inp = make_workload(T, seed, skew, device="cpu")
     t0 = time.perf_counter()
     oracle.moe_forward(*W.operator_args(inp), 0, 2.5, geo.n_group, geo.topk_group, geo.top_k)
     dt = time.perf_counter() - t0
@@ -505,6 +506,9 @@ def main():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--skew", type=int, default=0,
+                    help="route every token onto this many hot local experts (config 4: 8); "
+                         "0 = grouped top-k over random logits")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p",
@@ -544,7 +548,7 @@ def main():
     hbm_peak, bf16_peak, peak_src = load_peaks()
     fp8_peak = 2.0 * bf16_peak
     T = args.tokens
-    inp = make_workload(T, args.seed)
+    inp = make_workload(T, args.seed, args.skew)
     rows, active = routed_stats(inp)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
     fmoe_b200.kernel(*W.operator_args(inp), 0, 2.5)  # first call: library setup
@@ -587,9 +591,22 @@ def main():
                                       for i in range(5)])),
                 "layer_hbm_frac": round(layer_bytes(T, active) / (ms_per_step * 1e-3) / 1e9
                                         / hbm_peak, 3)}
+    tile_n = fmoe_b200.load_library().fmoe_autotune_tile_n(T)
+    if args.skew:
+        # compute-bound case: GEMM1 against the FP8 dense peak
+        g1_flops = rows * GEMM1_FLOP_PER_ROW
+        tf = g1_flops / (g1_ms * 1e-3) / 1e12
+        roofline.update({"bound": "tensor", "achieved": round(tf, 1), "peak": fp8_peak,
+                         "unit": "TFLOP/s", "frac": round(tf / fp8_peak, 3),
+                         "peak_source": peak_src + ", fp8 = 2 x bf16",
+                         "flops_per_launch": g1_flops})
+        roofline.pop("bytes_per_launch")
+    if tile_n == 128:
+        roofline["kernel"] = "grouped_gemm_tm_kernel<GEMM1+SwiGLU>"
     traffic_file = ROOT / "profiles" / "traffic.json"
     if traffic_file.exists():
-        tr = json.loads(traffic_file.read_text()).get(f"gemm1_T{T}")
+        key = f"gemm1_T{T}" + (f"_hot{args.skew}" if args.skew else "")
+        tr = json.loads(traffic_file.read_text()).get(key)
         if tr:
             roofline["traffic"] = tr
 
@@ -601,18 +618,21 @@ def main():
            "serial_value": round(T / (e2e_serial_ms * 1e-3), 1)}
 
     line = {
-        "metric": "MoE layer tokens/s (DS-V3 decode, T=64)", "value": round(value, 1),
+        "metric": ("MoE layer tokens/s (DS-V3 decode, T=64)" if not args.skew else
+                   f"MoE layer tokens/s (DS-V3, T={T}, {args.skew} hot experts)"),
+        "value": round(value, 1),
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_per_step, 4), "us_per_call": round(ms_per_step * 1e3, 1),
         "us_per_call_eager": round(statistics.mean(ms_eager) * 1e3, 1),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "e4m3 x e4m3 -> fp32 (tcgen05 kind::f8f6f4), fp32 block-scale promotion",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, FP8 128-block scales)",
-        "config": {"workload": f"config1_dsv3_decode_T{T}", "tokens_per_rank": T,
+        "config": {"workload": (f"config1_dsv3_decode_T{T}" if not args.skew else
+                                f"config4_dsv3_T{T}_hot{args.skew}"), "tokens_per_rank": T,
                    "hidden": 7168, "intermediate": 2048, "experts": 256, "local_experts": 32,
                    "top_k": 8, "n_group": 8, "topk_group": 4, "routed_rows": rows,
-                   "active_experts": active, "tile_n": fmoe_b200.load_library()
-                   .fmoe_autotune_tile_n(T), "parallelism": f"replicas x{world}",
+                   "active_experts": active, "tile_n": tile_n,
+                   "parallelism": f"replicas x{world}",
                    "l2": "flushed between calls (256 MiB write, then read back); weights > L2",
                    "launch": "one CUDA graph replay per step (memset + 5 PDL kernels)"},
         "roofline": roofline, "clocks": clocks, "e2e": e2e,
@@ -620,7 +640,7 @@ def main():
     }
     if rank == 0:
         if not args.no_cpu and world == 1:
-            line["cpu_baseline"] = cpu_baseline(T, args.seed)
+            line["cpu_baseline"] = cpu_baseline(T, args.seed, args.skew)
         if not args.no_sweep and world == 1:
             line["sweep"] = sweep(args.seed, hbm_peak, fp8_peak,
                                   tiles=tuple(int(x) for x in args.sweep_tiles.split(",")))
