@@ -618,7 +618,7 @@ def main():
            "serial_value": round(T / (e2e_serial_ms * 1e-3), 1)}
 
     line = {
-        "metric": ("MoE layer tokens/s (DS-V3 decode, T=64)" if not args.skew else
+        "metric": (f"MoE layer tokens/s (DS-V3 decode, T={T})" if not args.skew else
                    f"MoE layer tokens/s (DS-V3, T={T}, {args.skew} hot experts)"),
         "value": round(value, 1),
         "unit": "tokens/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
