@@ -145,22 +145,63 @@ __global__ void __launch_bounds__(256) scatter_gather_kernel(ScatterArgs a) {
     __syncthreads();
   }
   const int n = s_nlocal;
-  for (int v = tid; v < n * vw; v += blockDim.x) {
-    const int li = v / vw, pv = v - li * vw;
-    const int i = s_list[li];
-    const int tok = i / K;
-    const uint4 x = pre_rows ? s_pre[tok * vw + pv]
-                             : ld_nc_v4(a.hidden + (t0 + tok) * a.H + (v0 + pv) * 16);
-    *reinterpret_cast<uint4*>(a.a_perm + (int64_t)s_row[i] * a.H + (v0 + pv) * 16) = x;
+  if (pre_rows) {
+    for (int v = tid; v < n * vw; v += blockDim.x) {
+      const int li = v / vw, pv = v - li * vw;
+      const int i = s_list[li];
+      *reinterpret_cast<uint4*>(a.a_perm + (int64_t)s_row[i] * a.H + (v0 + pv) * 16) =
+          s_pre[(i / K) * vw + pv];
+    }
+  } else {
+    // kUnroll loads in flight per thread before their stores (a store may alias the next
+    // load, so the compiler would otherwise wait for each load in turn)
+    constexpr int kUnroll = 4;
+    for (int vb = tid; vb < n * vw; vb += kUnroll * blockDim.x) {
+      uint4 x[kUnroll];
+      int64_t dst[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int v = vb + u * blockDim.x;
+        dst[u] = -1;
+        if (v < n * vw) {
+          const int li = v / vw, pv = v - li * vw;
+          const int i = s_list[li];
+          x[u] = ld_nc_v4(a.hidden + (t0 + i / K) * a.H + (v0 + pv) * 16);
+          dst[u] = (int64_t)s_row[i] * a.H + (v0 + pv) * 16;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+        if (dst[u] >= 0) *reinterpret_cast<uint4*>(a.a_perm + dst[u]) = x[u];
+    }
   }
   if (kbw > 0) {
-    for (int v = tid; v < n * kbw; v += blockDim.x) {
-      const int li = v / kbw, bb = v - li * kbw;
-      const int i = s_list[li];
-      const int tok = i / K;
-      a.a_scale[(int64_t)(kb0 + bb) * a.row_cap + s_row[i]] =
-          pre_scales ? s_pscale[tok * kbw + bb]
-                     : a.hidden_scale[(int64_t)(kb0 + bb) * a.T + t0 + tok];
+    if (pre_scales) {
+      for (int v = tid; v < n * kbw; v += blockDim.x) {
+        const int li = v / kbw, bb = v - li * kbw;
+        const int i = s_list[li];
+        a.a_scale[(int64_t)(kb0 + bb) * a.row_cap + s_row[i]] = s_pscale[(i / K) * kbw + bb];
+      }
+    } else {
+      constexpr int kUnroll = 4;
+      for (int vb = tid; vb < n * kbw; vb += kUnroll * blockDim.x) {
+        float x[kUnroll];
+        int64_t dst[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int v = vb + u * blockDim.x;
+          dst[u] = -1;
+          if (v < n * kbw) {
+            const int li = v / kbw, bb = v - li * kbw;
+            const int i = s_list[li];
+            x[u] = __ldg(a.hidden_scale + (int64_t)(kb0 + bb) * a.T + t0 + i / K);
+            dst[u] = (int64_t)(kb0 + bb) * a.row_cap + s_row[i];
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u)
+          if (dst[u] >= 0) a.a_scale[dst[u]] = x[u];
+      }
     }
   }
   // padding rows of the experts this CTA column owns (expert e goes to x = e % gridDim.x)
@@ -197,29 +238,44 @@ __global__ void __launch_bounds__(128) combine_kernel(CombineArgs a) {
   pdl_trigger();
   if (threadIdx.x < a.top_k) s_rows[threadIdx.x] = a.token_row[t * a.top_k + threadIdx.x];
   __syncthreads();
-  // this CTA covers 8-element vectors [blockIdx.y * 128, +128) of the token's row
+  // this CTA covers 8-element vectors [blockIdx.y * 128 * kCombineVec, + 128 * kCombineVec)
+  // of the token's row; thread i takes vectors i, i + 128, ..., so each route's row is read
+  // with kCombineVec independent loads in flight
   const int nv = a.H / 8;
-  const int vend = min(nv, (int)(blockIdx.y + 1) * 128);
-  for (int v = blockIdx.y * 128 + threadIdx.x; v < vend; v += blockDim.x) {
-    float acc[8];
+  const int vb = (int)blockIdx.y * 128 * kCombineVec + (int)threadIdx.x;
+  float acc[kCombineVec][8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-    for (int k = 0; k < a.top_k; ++k) {
-      const int row = s_rows[k];
-      if (row < 0) continue;
-      const uint4 x = ld_nc_v4(a.ow + (int64_t)row * a.H + v * 8);
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&x);
+  for (int u = 0; u < kCombineVec; ++u)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[u][j] = 0.0f;
+  for (int k = 0; k < a.top_k; ++k) {
+    const int row = s_rows[k];
+    if (row < 0) continue;
+    uint4 x[kCombineVec];
+#pragma unroll
+    for (int u = 0; u < kCombineVec; ++u) {
+      const int v = vb + u * 128;
+      x[u] = v < nv ? ld_nc_v4(a.ow + (int64_t)row * a.H + v * 8) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kCombineVec; ++u) {
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&x[u]);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float2 f = __bfloat1622float2(h[j]);
-        acc[2 * j] += f.x;
-        acc[2 * j + 1] += f.y;
+        acc[u][2 * j] += f.x;
+        acc[u][2 * j + 1] += f.y;
       }
     }
+  }
+#pragma unroll
+  for (int u = 0; u < kCombineVec; ++u) {
+    const int v = vb + u * 128;
+    if (v >= nv) continue;
     uint4 o;
     __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[2 * j], acc[2 * j + 1]);
+    for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[u][2 * j], acc[u][2 * j + 1]);
     *reinterpret_cast<uint4*>(a.out + t * a.H + v * 8) = o;
   }
 }

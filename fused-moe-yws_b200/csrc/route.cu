@@ -334,26 +334,57 @@ __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
   // ---- last CTA: expert totals, per-CTA bases, 16-row aligned offsets, chunks ----
   // cta_base[c][e] = rows of expert e routed by CTAs before c (relative to the expert's
   // first row; the scatter adds expert_off[e])
-  for (int e = warp; e < a.E_local; e += kWarps) {
-    int run = 0;
-    if (nctas == 1) {
-      run = s_cnt[e];
-      if (lane == 0) a.cta_base[e] = 0;
-    } else {
-      for (int c0 = 0; c0 < nctas; c0 += 32) {
-        const int c = c0 + lane;
-        const int v = c < nctas ? __ldcg(a.cta_counts + (int64_t)c * a.E_local + e) : 0;
-        int incl = v;
+  if (nctas == 1) {
+    for (int e = threadIdx.x; e < a.E_local; e += blockDim.x) {
+      a.cta_base[e] = 0;
+      s_tot[e] = s_cnt[e];
+    }
+  } else {
+    // Warp w owns CTAs [c0, c1) and lane l experts l, l + 32, ...: each count is read with
+    // coalesced loads issued kBatch at a time, so the pass costs a few L2 round trips
+    // rather than one per 32 CTAs. Pass 1 sums each warp's range, a scan over the warps
+    // gives each range its start, pass 2 writes the bases.
+    constexpr int kBatch = 16;
+    int* s_part = reinterpret_cast<int*>(&s_sc[0][0]);  // [kWarps][E_local], scores are done
+    const int c0 = (int)((int64_t)nctas * warp / kWarps);
+    const int c1 = (int)((int64_t)nctas * (warp + 1) / kWarps);
+    for (int e = lane; e < a.E_local; e += 32) {
+      int sum = 0;
+      for (int cb = c0; cb < c1; cb += kBatch) {
+        int v[kBatch];
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const int y = __shfl_up_sync(0xffffffffu, incl, o);
-          if (lane >= o) incl += y;
+        for (int q = 0; q < kBatch; ++q)
+          v[q] = cb + q < c1 ? __ldcg(a.cta_counts + (int64_t)(cb + q) * a.E_local + e) : 0;
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) sum += v[q];
+      }
+      s_part[warp * a.E_local + e] = sum;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < a.E_local; e += blockDim.x) {
+      int run = 0;
+      for (int w = 0; w < kWarps; ++w) {
+        const int v = s_part[w * a.E_local + e];
+        s_part[w * a.E_local + e] = run;
+        run += v;
+      }
+      s_tot[e] = run;
+    }
+    __syncthreads();
+    for (int e = lane; e < a.E_local; e += 32) {
+      int run = s_part[warp * a.E_local + e];
+      for (int cb = c0; cb < c1; cb += kBatch) {
+        int v[kBatch];
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q)
+          v[q] = cb + q < c1 ? __ldcg(a.cta_counts + (int64_t)(cb + q) * a.E_local + e) : 0;
+#pragma unroll
+        for (int q = 0; q < kBatch; ++q) {
+          if (cb + q < c1) a.cta_base[(int64_t)(cb + q) * a.E_local + e] = run;
+          run += v[q];
         }
-        if (c < nctas) a.cta_base[(int64_t)c * a.E_local + e] = run + incl - v;
-        run += __shfl_sync(0xffffffffu, incl, 31);
       }
     }
-    if (lane == 0) s_tot[e] = run;
   }
   __syncthreads();
   if (warp == 0) {
