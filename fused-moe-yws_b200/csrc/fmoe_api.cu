@@ -407,10 +407,14 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   ca.T = T;
   ca.H = H;
   ca.top_k = p->top_k;
-  FMOE_CUDA_TRY(launch_pdl(combine_kernel,
-                           dim3((unsigned)T, (unsigned)((H / 8 + 128 * kCombineVec - 1) /
-                                                        (128 * kCombineVec))),
-                           dim3(128), 0, stream, ca));
+  if (T >= kCombineWideTokens)
+    FMOE_CUDA_TRY(launch_pdl(combine_kernel<2>,
+                             dim3((unsigned)T, (unsigned)((H / 8 + 255) / 256)), dim3(128), 0,
+                             stream, ca));
+  else
+    FMOE_CUDA_TRY(launch_pdl(combine_kernel<1>,
+                             dim3((unsigned)T, (unsigned)((H / 8 + 127) / 128)), dim3(128), 0,
+                             stream, ca));
   return mark_stage(5, stream);
 }
 }  // namespace

@@ -100,9 +100,11 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 
 __global__ void route_plan_kernel(RouteArgs a);
 __global__ void scatter_gather_kernel(ScatterArgs a);
-// combine_kernel: grid (T, ceil(H / 8 / (128 * kCombineVec))), 128 threads; each thread
-// sums kCombineVec 16-byte vectors of its token's row.
-constexpr int kCombineVec = 2;
+// combine_kernel<V>: grid (T, ceil(H / 8 / (128 * V))), 128 threads; each thread sums V
+// 16-byte vectors of its token's row. V = 1 below kCombineWideTokens tokens (latency-bound:
+// more CTAs), V = 2 from there on (more loads in flight per thread).
+constexpr int64_t kCombineWideTokens = 512;
+template <int V>
 __global__ void combine_kernel(CombineArgs a);
 
 // Grouped GEMM launchers (gemm_sm100.cu). `bn` selects the token tile; returns a CUDA error.

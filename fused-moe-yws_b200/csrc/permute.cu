@@ -231,6 +231,7 @@ __global__ void __launch_bounds__(256) scatter_gather_kernel(ScatterArgs a) {
   }
 }
 
+template <int kCombineVec>
 __global__ void __launch_bounds__(128) combine_kernel(CombineArgs a) {
   __shared__ int s_rows[32];
   const int64_t t = blockIdx.x;
@@ -279,5 +280,8 @@ __global__ void __launch_bounds__(128) combine_kernel(CombineArgs a) {
     *reinterpret_cast<uint4*>(a.out + t * a.H + v * 8) = o;
   }
 }
+
+template __global__ void combine_kernel<1>(CombineArgs a);
+template __global__ void combine_kernel<2>(CombineArgs a);
 
 }  // namespace fmoe
