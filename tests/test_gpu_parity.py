@@ -121,7 +121,7 @@ TINY_LOCAL = W.Geometry(hidden=256, inter=128, num_experts=16, num_local=8, n_gr
                         topk_group=2, top_k=4)
 
 
-@pytest.mark.parametrize("T", [1, 2, 16, 33, 100])
+@pytest.mark.parametrize("T", [1, 2, 16, 33, 100, 600])
 @pytest.mark.parametrize("geo,offset", [(W.TINY, 0), (TINY_LOCAL, 8), (TINY_LOCAL, 0)],
                          ids=["tiny", "tiny_slice8", "tiny_slice0"])
 def test_forward_tiny(fmoe, oracle_mod, T, geo, offset):
@@ -177,8 +177,11 @@ def test_forward_tiny_throughput_family(fmoe, oracle_mod, T, geo, offset):
     assert _device_error(fmoe, geo, T, offset, tile_n=128) == 0
 
 
-@pytest.mark.parametrize("T", [777, 64, 17, 1])
+@pytest.mark.parametrize("T", [20011, 8192, 777, 64, 17, 1])
 def test_plan_bitexact(fmoe, oracle_mod, T):
+    """The permutation plan (expert counts and offsets, row <-> token maps) bit for bit against
+    the oracle. The large T cases give the routing kernel's last CTA several batches of
+    per-CTA counts per warp (512 and 1,251 CTAs), the last one partial."""
     geo = W.DSV3
     gpu, cpu, _ = _inputs(geo, T, seed=4)
     _run(fmoe, geo, gpu, 0, 2.5)
