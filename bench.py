@@ -303,15 +303,19 @@ def cpu_baseline(T, seed, skew=0):
             "sample": f"one call of the T={T} DS-V3 layer (dequantise + fp32 GEMMs), {dt:.2f} s"}
 
 
-def sweep(seed, hbm_peak, fp8_peak, tiles=(0,)):
+def sweep(seed, hbm_peak, fp8_peak, tiles=(0,), tokens=None):
     """Configs 1, 2 and 4 over T; `tiles` lists the token tiles timed per case (0 = the
-    autotune table). Tiles above 16 are skipped for T < 64 and 128 for T < 512."""
+    autotune table). Tiles above 16 are skipped for T < 64 and 128 for T < 512. `tokens`
+    replaces the cases by uniform-routing ones at those token counts."""
     res = []
     lib = fmoe_b200.load_library()
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
-    for cfg, T, skew in [("config1", 1, 0), ("config1", 4, 0), ("config1", 16, 0),
-                         ("config1", 64, 0), ("config2", 512, 0), ("config2", 2048, 0),
-                         ("config2", 4096, 0), ("config2", 8192, 0), ("config4", 4096, 8)]:
+    cases = [("config1", 1, 0), ("config1", 4, 0), ("config1", 16, 0), ("config1", 64, 0),
+             ("config2", 512, 0), ("config2", 2048, 0), ("config2", 4096, 0),
+             ("config2", 8192, 0), ("config4", 4096, 8)]
+    if tokens:
+        cases = [("config1" if T <= 64 else "config2", T, 0) for T in tokens]
+    for cfg, T, skew in cases:
         inp = make_workload(T, seed, skew)
         rows, active = routed_stats(inp)
         b = layer_bytes(T, active)
@@ -515,6 +519,8 @@ def main():
                     help="expert-parallel runs (N > 1): rows over peer memory or NCCL all-to-all")
     ap.add_argument("--sweep-tiles", default="0",
                     help="comma-separated token tiles timed per sweep case (0 = autotune)")
+    ap.add_argument("--sweep-tokens", default="",
+                    help="comma-separated token counts replacing the sweep's cases")
     args = ap.parse_args()
     args.tokens_set = args.tokens is not None
     if args.tokens is None:
@@ -643,7 +649,8 @@ def main():
             line["cpu_baseline"] = cpu_baseline(T, args.seed, args.skew)
         if not args.no_sweep and world == 1:
             line["sweep"] = sweep(args.seed, hbm_peak, fp8_peak,
-                                  tiles=tuple(int(x) for x in args.sweep_tiles.split(",")))
+                                  tiles=tuple(int(x) for x in args.sweep_tiles.split(",")),
+                                  tokens=[int(x) for x in args.sweep_tokens.split(",") if x])
             line["sweep_fp8_peak_tflops"] = fp8_peak
         emit(line)
     if world > 1:

@@ -19,7 +19,7 @@ struct TileChoice {
 
 constexpr TileChoice kAutotuneTable[] = {
     {256, 16},
-    {2048, 64},
+    {896, 64},
     {INT64_MAX, 128},
 };
 
