@@ -8,15 +8,19 @@
 // accumulator; an epilogue thread owns one token row, so the block-scale promotion is a
 // single FMA per element with a per-thread scalar (token scale x weight-block scale).
 //   GEMM1: N = 128 gate rows [128 m, 128 m + 128) + the matching 128 up rows of W13; the
-//          thread holding token row r and C columns [32 j, 32 j + 32) reads gate columns
-//          32 j.. and up columns 128 + 32 j..: SwiGLU is thread-local; the per-(token,
-//          128-column) amax is combined across the 4 column slices through shared memory.
-//   GEMM2: N = 256 rows of W2 (two 128-row scale blocks); the thread owns 64 consecutive
-//          output columns of its token row and stores them as 128 contiguous bytes.
+//          thread holding token row r and C columns [64 j, 64 j + 64) reads gate columns
+//          64 j.. and up columns 128 + 64 j..: SwiGLU is thread-local; the per-(token,
+//          128-column) amax is combined across the 2 column slices through shared memory.
+//   GEMM2: N = 256 rows of W2 (two 128-row scale blocks); the thread owns 128 consecutive
+//          output columns of its token row (one scale block) and stores them as 256
+//          contiguous bytes.
 // Warps: 0 TMA producer (also stages each tile's weight-scale rows into a 2-slot ring),
-// 1 TMEM allocator + MMA issuer, 2..17 epilogue (TMEM lane quadrant = warp % 4, column
-// slice = (warp - 2) / 4). Two 256-column TMEM accumulators let the MMA of K block kb+1
-// overlap the promotion of kb. The schedule (data-parallel waves, stream-K tail), bounded
+// 1 TMEM allocator + MMA issuer, 2..9 epilogue (TMEM lane quadrant = warp % 4, column
+// slice = (warp - 2) / 4). Ten warps put at most three on an SM sub-partition, so a thread
+// can hold 168 registers: its 128 accumulators stay in registers, and the per-step waits,
+// fences and barrier arrivals are paid by 8 warps instead of 16 (18 warps capped a thread
+// at 96 registers, which put spills on the K loop; measured 3-12 % slower).
+// Two 256-column TMEM accumulators let the MMA of K block kb+1 overlap the promotion of kb. The schedule (data-parallel waves, stream-K tail), bounded
 // waits, abort protocol and error reporting are those of gemm_sm100.cu.
 #include <cuda_fp8.h>
 
@@ -31,8 +35,8 @@ using namespace sm100;
 
 namespace {
 
-constexpr int kTmThreads = 576;     // 18 warps
-constexpr int kTmEpiThreads = 512;  // warps 2..17
+constexpr int kTmThreads = 320;     // 10 warps
+constexpr int kTmEpiThreads = 256;  // warps 2..9
 constexpr int kTmBarAll = 1;        // named barrier over the epilogue warps
 constexpr int kTmSmemLimit = 232448;
 
@@ -63,8 +67,8 @@ struct TmCfg {
 // fast division: the reference is built with --use_fast_math, which approximates it too
 __device__ __forceinline__ float silu_tm(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
-// acc[i] += D[i] * s, 16 TMEM columns per load (the thread's 64 accumulators leave room
-// for 16 loaded values), as packed FMAs (each lane of fma.rn.f32x2 rounds like fmaf).
+// acc[i] += D[i] * s, 16 TMEM columns per load (beside the thread's 128 accumulators),
+// as packed FMAs (each lane of fma.rn.f32x2 rounds like fmaf).
 template <int N>
 __device__ __forceinline__ void promote_tm(float (&acc)[N], uint32_t taddr, float s) {
   const float2 s2 = make_float2(s, s);
@@ -166,15 +170,15 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     }
     for (int b = 0; b < NB; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 16);
+      mbar_init(&tempty[b], kTmEpiThreads / 32);
     }
     for (int r = 0; r < SR; ++r) {
       mbar_init(&sfull[r], 1);
-      mbar_init(&sempty[r], 16);
+      mbar_init(&sempty[r], kTmEpiThreads / 32);
     }
     for (int r = 0; r < 2; ++r) {
       mbar_init(&wfull[r], 32);
-      mbar_init(&wempty[r], 16);
+      mbar_init(&wempty[r], kTmEpiThreads / 32);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -359,14 +363,14 @@ __global__ void __launch_bounds__(kTmThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ epilogue
-    const int ew = warp - 2;        // 0..15
+    const int ew = warp - 2;        // 0..7
     const int q = warp & 3;         // TMEM lane quadrant = token rows 32 q .. 32 q + 31
-    const int j = ew >> 2;          // column slice 0..3
+    const int j = ew >> 2;          // column slice 0..1
     const int tid_e = ew * 32 + lane;
     const int row = q * 32 + lane;  // token row inside the tile
-    constexpr int NA = kG1 ? 32 : 64;
+    constexpr int NA = kG1 ? 64 : 128;
     float acc[NA];
-    float acc_u[kG1 ? 32 : 1];
+    float acc_u[kG1 ? 64 : 1];
     int it = 0, wseg = 0;
     bool ok = true;
     for (;;) {
@@ -390,7 +394,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       for (int i = 0; i < NA; ++i) acc[i] = 0.0f;
       if constexpr (kG1) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) acc_u[i] = 0.0f;
+        for (int i = 0; i < 64; ++i) acc_u[i] = 0.0f;
       }
       {
         // the descriptor fields are re-read from shared memory where needed, so no
@@ -410,10 +414,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         } else {
           const float* pp = args.partials + (int64_t)(2 * role.cl) * C::kPartialFloats + row * 256;
           if constexpr (kG1) {
-            load_vec<32>(acc, pp + 32 * j);
-            load_vec<32>(acc_u, pp + 128 + 32 * j);
-          } else {
             load_vec<64>(acc, pp + 64 * j);
+            load_vec<64>(acc_u, pp + 128 + 64 * j);
+          } else {
+            load_vec<128>(acc, pp + 128 * j);
           }
         }
       }
@@ -431,10 +435,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         const float st = sring[slot * 128 + row];  // token scale (rows >= ncols: unused)
         const uint32_t tb = tmem + ((uint32_t)(q * 32) << 16) + b * 256;
         if constexpr (kG1) {
-          promote_tm<32>(acc, tb + 32 * j, st * wrow[ks]);
-          promote_tm<32>(acc_u, tb + 128 + 32 * j, st * wrow[kMaxKSteps + ks]);
+          promote_tm<64>(acc, tb + 64 * j, st * wrow[ks]);
+          promote_tm<64>(acc_u, tb + 128 + 64 * j, st * wrow[kMaxKSteps + ks]);
         } else {
-          promote_tm<64>(acc, tb + 64 * j, st * wrow[(j >= 2) * kMaxKSteps + ks]);
+          promote_tm<128>(acc, tb + 128 * j, st * wrow[j * kMaxKSteps + ks]);
         }
         tc_fence_before();
         __syncwarp();
@@ -465,10 +469,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
           float* part =
               args.partials + (int64_t)(2 * cta + role.slot) * C::kPartialFloats + row * 256;
           if constexpr (kG1) {
-            store_vec<32>(part + 32 * j, acc);
-            store_vec<32>(part + 128 + 32 * j, acc_u);
-          } else {
             store_vec<64>(part + 64 * j, acc);
+            store_vec<64>(part + 128 + 64 * j, acc_u);
+          } else {
+            store_vec<128>(part + 128 * j, acc);
           }
           named_bar(kTmBarAll, kTmEpiThreads);
           if (tid_e == 0) red_release_add(args.tile_counters + role.cf, k1 - k0);
@@ -481,10 +485,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         const int slot = role.slot;
         float* part = args.partials + (int64_t)(2 * cta + slot) * C::kPartialFloats + row * 256;
         if constexpr (kG1) {
-          store_vec<32>(part + 32 * j, acc);
-          store_vec<32>(part + 128 + 32 * j, acc_u);
-        } else {
           store_vec<64>(part + 64 * j, acc);
+          store_vec<64>(part + 128 + 64 * j, acc_u);
+        } else {
+          store_vec<128>(part + 128 * j, acc);
         }
         __threadfence();
         named_bar(kTmBarAll, kTmEpiThreads);
@@ -499,10 +503,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         if (!*last_flag) continue;
         __threadfence();
         if constexpr (kG1) {
-          sum_tm<32>(acc, args.partials, row * 256 + 32 * j, sk, tile_begin, cf, cl);
-          sum_tm<32>(acc_u, args.partials, row * 256 + 128 + 32 * j, sk, tile_begin, cf, cl);
-        } else {
           sum_tm<64>(acc, args.partials, row * 256 + 64 * j, sk, tile_begin, cf, cl);
+          sum_tm<64>(acc_u, args.partials, row * 256 + 128 + 64 * j, sk, tile_begin, cf, cl);
+        } else {
+          sum_tm<128>(acc, args.partials, row * 256 + 128 * j, sk, tile_begin, cf, cl);
         }
       }
 
@@ -512,21 +516,23 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         // ---- SwiGLU, then FP8 hi/lo on one per-(token, 128-column) scale ----
         float amax = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < 64; ++i) {
           acc[i] = acc[i] * silu_tm(acc_u[i]);
           amax = fmaxf(amax, fabsf(acc[i]));
         }
         ax[j * 128 + row] = amax;
         named_bar(kTmBarAll, kTmEpiThreads);
-        amax = fmaxf(fmaxf(ax[row], ax[128 + row]), fmaxf(ax[256 + row], ax[384 + row]));
+        amax = fmaxf(ax[row], ax[128 + row]);
         if (real) {
           const float inv = amax > 0.0f ? 448.0f / amax : 0.0f;
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
           uint32_t hi[8], lo[8];
 #pragma unroll
           for (int k = 0; k < 32; k += 4) {
             float x[4], h[4], l[4];
 #pragma unroll
-            for (int u = 0; u < 4; ++u) x[u] = acc[k + u] * inv;
+            for (int u = 0; u < 4; ++u) x[u] = acc[32 * hh + k + u] * inv;
             const __nv_fp8x2_storage_t h01 =
                 __nv_cvt_float2_to_fp8x2(make_float2(x[0], x[1]), __NV_SATFINITE, __NV_E4M3);
             const __nv_fp8x2_storage_t h23 =
@@ -548,20 +554,21 @@ __global__ void __launch_bounds__(kTmThreads, 1)
           // full 32-byte sectors (the workspace is 256-byte aligned, 2I a multiple of 256):
           // 16-byte stores scattered over 32 rows per instruction stalled the epilogue for
           // microseconds per tile while the TMA loads saturated the memory system
-          uint8_t* dst = args.cq + grow * (2 * (int64_t)args.I) + m * 256 + j * 32;
+          uint8_t* dst = args.cq + grow * (2 * (int64_t)args.I) + m * 256 + j * 64 + 32 * hh;
           st_global_v8(dst, hi);
           st_global_v8(dst + 128, lo);
+          }
           if (j == 0) args.c_scale[(int64_t)m * args.row_cap + grow] = amax / 448.0f;
         }
         named_bar(kTmBarAll, kTmEpiThreads);  // ax is reused by the next tile
       } else {
-        // ---- weighted expert output: 64 consecutive bf16 of this token row ----
+        // ---- weighted expert output: 128 consecutive bf16 of this token row ----
         if (real) {
           const float w = __ldg(args.row_w + grow);
           // 32-byte stores: full sectors (H is a multiple of 256 on this path)
-          __nv_bfloat16* dst = args.ow + grow * args.H + m * 256 + 64 * j;
+          __nv_bfloat16* dst = args.ow + grow * args.H + m * 256 + 128 * j;
 #pragma unroll
-          for (int v = 0; v < 4; ++v) {
+          for (int v = 0; v < 8; ++v) {
             uint32_t o[8];
 #pragma unroll
             for (int u = 0; u < 8; ++u) {
