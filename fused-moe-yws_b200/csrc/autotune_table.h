@@ -19,7 +19,7 @@ struct TileChoice {
 
 constexpr TileChoice kAutotuneTable[] = {
     {256, 16},
-    {896, 64},
+    {768, 64},
     {INT64_MAX, 128},
 };
 

@@ -150,7 +150,7 @@ def test_forward_dsv3_every_tile(fmoe, oracle_mod, tile_n):
     assert _device_error(fmoe, geo, T, tile_n=tile_n) == 0
 
 
-# tile 0 = the autotune table (decode family up to 896 tokens, throughput family above);
+# tile 0 = the autotune table (decode family up to 768 tokens, throughput family above);
 # the explicit tiles force the other family on the same inputs
 @pytest.mark.parametrize("T,skew,tile", [(512, 0, 0), (4096, 0, 0), (8192, 0, 0), (4096, 8, 0),
                                          (4096, 0, 64), (4096, 8, 64), (1024, 0, 128)],
