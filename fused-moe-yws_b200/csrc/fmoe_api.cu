@@ -32,6 +32,7 @@ namespace {
 thread_local std::string g_last_error;
 thread_local cudaEvent_t g_stage_events[6] = {nullptr, nullptr, nullptr, nullptr, nullptr, nullptr};
 thread_local bool g_stage_on = false;
+thread_local int g_inject_err = 0;  // fmoe_selftest_inject_device_error, next forward call
 
 int mark_stage(int i, cudaStream_t s);
 
@@ -94,11 +95,8 @@ int validate(const fmoe_problem* p) {
   return FMOE_OK;
 }
 
-// Token tile of a call: the caller's choice, else the committed table; the throughput
-// family (128) needs GEMM2's 256-row weight tiles to divide hidden_size.
 int tile_n_of(const fmoe_problem* p) {
-  const int bn = p->tile_n != 0 ? p->tile_n : autotune_tile_n(p->num_tokens);
-  return bn == 128 && p->hidden_size % 256 != 0 ? 64 : bn;
+  return resolve_tile_n(p->tile_n, p->num_tokens, p->hidden_size);
 }
 
 bool aligned(const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; }
@@ -161,6 +159,49 @@ int num_sms_current() {
   return cache[dev];
 }
 
+// ---------------------------------------------------------------------- error sink
+// One host-mapped pinned pair {error bits, report count} per device. The combine kernel of
+// every call adds its call's device error word to it (report_device_error), so a timeout
+// inside a GEMM reaches the host without a synchronisation: fmoe_poll_device_error() reads
+// the pair. It is allocated on a device's first call that is not being captured into a
+// graph (a capturing stream cannot allocate); calls captured before that report nothing.
+struct ErrorSink {
+  unsigned* host = nullptr;  // [0] bits, [1] count
+  unsigned* dev = nullptr;
+  unsigned seen = 0;         // count at the last poll
+};
+std::mutex g_sink_mu;
+ErrorSink g_sinks[64];
+
+unsigned* error_sink_for(int dev, cudaStream_t stream) {
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(g_sink_mu);
+  ErrorSink& s = g_sinks[dev];
+  if (s.dev) return s.dev;
+  if (stream) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone)
+      return nullptr;
+  }
+  void* h = nullptr;
+  if (cudaHostAlloc(&h, 2 * sizeof(unsigned), cudaHostAllocMapped | cudaHostAllocPortable) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return nullptr;
+  }
+  void* d = nullptr;
+  if (cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFreeHost(h);
+    return nullptr;
+  }
+  s.host = static_cast<unsigned*>(h);
+  s.host[0] = 0;
+  s.host[1] = 0;
+  s.dev = static_cast<unsigned*>(d);
+  return s.dev;
+}
+
 int mark_stage(int i, cudaStream_t s) {
   if (!g_stage_on) return FMOE_OK;
   FMOE_CUDA_TRY(cudaEventRecord(g_stage_events[i], s));
@@ -192,6 +233,7 @@ RouteArgs route_args(const fmoe_problem* p, const Carved& c, const float* logits
   RouteArgs a;
   a.in_idx = nullptr;
   a.in_w = nullptr;
+  a.inject_err = 0;
   a.logits = logits;
   a.bias = static_cast<const uint16_t*>(bias);
   a.T = p->num_tokens;
@@ -220,13 +262,14 @@ RouteArgs route_args(const fmoe_problem* p, const Carved& c, const float* logits
 
 int launch_route(const fmoe_problem* p, const Carved& c, const float* logits, const void* bias,
                  int bn, cudaStream_t stream, const int* in_idx = nullptr,
-                 const float* in_w = nullptr) {
+                 const float* in_w = nullptr, int inject_err = 0) {
   // meta words and the stream-K counters are contiguous: one small memset per call
   FMOE_CUDA_TRY(cudaMemsetAsync(c.at<int>(c.L.meta), 0, c.L.counters - c.L.meta +
                                 kTileCounters * sizeof(int), stream));
   RouteArgs ra = route_args(p, c, logits, bias, bn);
   ra.in_idx = in_idx;
   ra.in_w = in_w;
+  ra.inject_err = inject_err;
   FMOE_CUDA_TRY(launch_pdl(route_plan_kernel, dim3((unsigned)c.L.n_route_ctas),
                            dim3(kRouteTokensPerCta * 32), 0, stream, ra));
   return FMOE_OK;
@@ -287,8 +330,13 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   const int64_t T = p->num_tokens;
   const int H = p->hidden_size, I = p->intermediate_size, EL = p->num_local_experts;
 
+  int dev = 0;
+  FMOE_CUDA_TRY(cudaGetDevice(&dev));
+  unsigned* sink = error_sink_for(dev, stream);
+  const int inject = g_inject_err;
+  g_inject_err = 0;
   if ((v = mark_stage(0, stream)) != FMOE_OK) return v;
-  v = launch_route(p, c, t->routing_logits, t->routing_bias, bn, stream, in_idx, in_w);
+  v = launch_route(p, c, t->routing_logits, t->routing_bias, bn, stream, in_idx, in_w, inject);
   if (v != FMOE_OK) return v;
   if ((v = mark_stage(1, stream)) != FMOE_OK) return v;
 
@@ -407,6 +455,8 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   ca.T = T;
   ca.H = H;
   ca.top_k = p->top_k;
+  ca.err_word = g.err;
+  ca.err_sink = sink;
   if (T >= kCombineWideTokens)
     FMOE_CUDA_TRY(launch_pdl(combine_kernel<2>,
                              dim3((unsigned)T, (unsigned)((H / 8 + 255) / 256)), dim3(128), 0,
@@ -483,7 +533,8 @@ int forward_cached(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* 
                    void* stream_ptr) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-  if (!graph_cache_enabled() || g_stage_on || !p || !t || p->num_tokens <= 0 ||
+  if (!graph_cache_enabled() || g_stage_on || g_inject_err != 0 || !p || !t ||
+      p->num_tokens <= 0 ||
       cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone)
     return run_forward(p, t, in_idx, in_w, workspace, workspace_bytes, stream_ptr);
   GraphKey key;
@@ -621,6 +672,35 @@ extern "C" int fmoe_read_device_error(const fmoe_problem* p, void* workspace, vo
     std::snprintf(buf, sizeof(buf), "device error word 0x%x", host);
     g_last_error = buf;
   }
+  return FMOE_OK;
+}
+
+extern "C" int fmoe_poll_device_error(int32_t* device_error) {
+  if (!device_error) return fail(FMOE_ERR_VALUE, "device_error must not be NULL");
+  *device_error = 0;
+  int dev = 0;
+  FMOE_CUDA_TRY(cudaGetDevice(&dev));
+  if (!error_sink_for(dev, nullptr))
+    return fail(FMOE_ERR_RUNTIME, "could not allocate the host-mapped device error word");
+  std::lock_guard<std::mutex> lock(g_sink_mu);
+  ErrorSink& s = g_sinks[dev];
+  volatile unsigned* h = s.host;
+  const unsigned count = h[1];
+  if (count == s.seen) return FMOE_OK;
+  s.seen = count;
+  unsigned bits = h[0];
+  h[0] = 0;
+  // a report whose bits were cleared by a racing poll still counts
+  *device_error = (int32_t)(bits != 0 ? bits : 0x40000000u);
+  char buf[128];
+  std::snprintf(buf, sizeof(buf), "device error word 0x%x reported by a call on device %d",
+                (unsigned)*device_error, dev);
+  g_last_error = buf;
+  return FMOE_OK;
+}
+
+extern "C" int fmoe_selftest_inject_device_error(int32_t bits) {
+  g_inject_err = bits;
   return FMOE_OK;
 }
 

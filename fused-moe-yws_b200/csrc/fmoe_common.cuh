@@ -69,9 +69,11 @@ inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
 inline WorkspaceLayout make_layout(const Geometry& g) {
   WorkspaceLayout L{};
-  const int64_t k_local = g.top_k < g.E_local ? g.top_k : g.E_local;
-  L.row_cap = (int64_t)align_up((size_t)(g.T * k_local + (int64_t)kRowAlign * g.E_local), 256);
-  L.max_chunks = g.E_local + (g.T * k_local) / kRowAlign + 1;
+  // Every (token, k) pair makes at most one routed row, and padding adds fewer than
+  // kRowAlign rows per expert, so the plan can never overflow row_cap or max_chunks, even
+  // when a caller's routing (fmoe_forward_routed) names one expert several times per token.
+  L.row_cap = (int64_t)align_up((size_t)(g.T * g.top_k + (int64_t)kRowAlign * g.E_local), 256);
+  L.max_chunks = g.E_local + (g.T * g.top_k) / kRowAlign + 1;
   L.n_route_ctas = (g.T + kRouteTokensPerCta - 1) / kRouteTokensPerCta;
   size_t off = 0;
   auto take = [&](size_t bytes) {

@@ -31,6 +31,7 @@ struct RouteArgs {
   int* expert_off;         // [E_local + 1]
   int* meta;               // [kMetaWords]
   Chunk* chunks;           // [max_chunks]
+  int inject_err;          // test hook: DeviceError bits CTA 0 ORs into the error word (0: none)
 };
 
 struct ScatterArgs {
@@ -79,7 +80,21 @@ struct CombineArgs {
   __nv_bfloat16* out;           // [T, H]
   int64_t T;
   int H, top_k;
+  const int* err_word;          // the call's device error word (meta[kMetaError])
+  unsigned* err_sink;           // host-mapped {bits, count} of the device, or null
 };
+
+// Host-mapped error sink, one per device: the combine kernel (the last kernel of every
+// call) adds a non-zero error word of its call to it with plain system-scope stores --
+// sink[0] |= bits, then sink[1] += 1 -- and the host polls it without synchronising.
+// Only the error path writes host memory; a clean call reads one word of its workspace.
+__device__ __forceinline__ void report_device_error(unsigned* sink, int bits) {
+  volatile unsigned* v = sink;
+  v[0] = v[0] | (unsigned)bits;
+  __threadfence_system();
+  v[1] = v[1] + 1u;
+  __threadfence_system();
+}
 
 // Launch with programmatic stream serialization (see pdl_wait / pdl_trigger).
 template <typename... KArgs, typename... Args>

@@ -237,6 +237,11 @@ __global__ void __launch_bounds__(128) combine_kernel(CombineArgs a) {
   const int64_t t = blockIdx.x;
   pdl_wait();
   pdl_trigger();
+  // every earlier kernel of the call has finished: pass its error word on to the host
+  if (a.err_sink && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0) {
+    const int e = *reinterpret_cast<const volatile int*>(a.err_word);
+    if (e != 0) report_device_error(a.err_sink, e);
+  }
   if (threadIdx.x < a.top_k) s_rows[threadIdx.x] = a.token_row[t * a.top_k + threadIdx.x];
   __syncthreads();
   // this CTA covers 8-element vectors [blockIdx.y * 128 * kCombineVec, + 128 * kCombineVec)

@@ -207,6 +207,8 @@ __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
   for (int i = threadIdx.x; i < a.E_local; i += blockDim.x) s_cnt[i] = 0;
   pdl_wait();
   pdl_trigger();
+  if (a.inject_err != 0 && blockIdx.x == 0 && threadIdx.x == 0)
+    atomicOr(a.meta + kMetaError, a.inject_err);
   __syncthreads();
 
   const int64_t t = (int64_t)blockIdx.x * kWarps + warp;

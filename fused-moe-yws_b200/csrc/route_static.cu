@@ -14,11 +14,16 @@
 //   * num_tokens <= kStaticRouteMaxTokens (8192) and num_local_experts <= 64; larger
 //     problems are rejected with FMOE_ERR_VALUE before anything is launched.
 //   * The first call on a device looks up the array's device address there
-//     (cudaGetSymbolAddress). Make that first call before any stream capture.
+//     (cudaGetSymbolAddress). Make that first call before any stream capture. The address
+//     is looked up again if the device's context has changed since (a device reset).
+//   * No device-side error word can be read back: within these limits the plan cannot
+//     overflow (at most num_tokens * top_k routed rows), which is the routing kernel's only
+//     error.
 //   * All calls share the one array and it keeps the last call's contents. The call
 //     clears the words that must start at zero. Calls that overlap on the GPU (different
 //     streams, or different host threads, without ordering between them) race on the
 //     array, so order them.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -58,16 +63,37 @@ int fail_static(int code, const std::string& msg) {
   return code;
 }
 
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+
+// The driver context current on this thread (nullptr if the entry point is unavailable).
+CUcontext current_context() {
+  static CtxGetCurrentFn fn = [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &ptr, 12000, cudaEnableDefault,
+                                         &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<CtxGetCurrentFn>(ptr);
+    return static_cast<CtxGetCurrentFn>(nullptr);
+  }();
+  CUcontext ctx = nullptr;
+  if (fn) fn(&ctx);
+  return ctx;
+}
+
 // Per-device address of g_route_scratch, looked up once per device with that device current.
+// The address belongs to the device's context: if that context was destroyed and a new one
+// created (cudaDeviceReset, for one), the address is looked up again in the new context.
 int scratch_address(unsigned char** out) {
   static std::mutex mu;
   static unsigned char* addr[64] = {nullptr};
+  static CUcontext ctx_of[64] = {nullptr};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail_static(FMOE_ERR_RUNTIME, cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return fail_static(FMOE_ERR_RUNTIME, "device index out of range");
   std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
+  if (!addr[dev] || ctx_of[dev] != current_context()) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_route_scratch);
     if (e != cudaSuccess)
@@ -75,6 +101,7 @@ int scratch_address(unsigned char** out) {
                          std::string("cudaGetSymbolAddress(g_route_scratch) failed: ") +
                              cudaGetErrorString(e));
     addr[dev] = static_cast<unsigned char*>(p);
+    ctx_of[dev] = current_context();  // the lookup made the device's context current
   }
   *out = addr[dev];
   return FMOE_OK;
@@ -108,10 +135,11 @@ extern "C" int fmoe_route_static(const fmoe_problem* p, const float* routing_log
   cudaError_t e = cudaMemsetAsync(scratch + kOffMeta, 0, kMetaWords * sizeof(int), stream);
   if (e != cudaSuccess) return fail_static(FMOE_ERR_RUNTIME, cudaGetErrorString(e));
 
-  const int bn = p->tile_n ? p->tile_n : autotune_tile_n(p->num_tokens);
+  const int bn = resolve_tile_n(p->tile_n, p->num_tokens, p->hidden_size);
   RouteArgs a;
   a.in_idx = nullptr;
   a.in_w = nullptr;
+  a.inject_err = 0;
   a.logits = routing_logits;
   a.bias = static_cast<const uint16_t*>(routing_bias);
   a.T = p->num_tokens;
@@ -125,8 +153,10 @@ extern "C" int fmoe_route_static(const fmoe_problem* p, const float* routing_log
   a.bn = bn;
   a.bn_log2 = 0;
   while ((1 << a.bn_log2) < bn) ++a.bn_log2;
-  const int64_t k_local = p->top_k < p->num_local_experts ? p->top_k : p->num_local_experts;
-  a.row_cap = p->num_tokens * k_local + (int64_t)kRowAlign * p->num_local_experts;
+  // T * top_k routed rows at most (the same bound as make_layout), so the plan never
+  // overflows and the routing kernel sets no device error word here; this entry point has
+  // no way to report one.
+  a.row_cap = p->num_tokens * p->top_k + (int64_t)kRowAlign * p->num_local_experts;
   a.max_chunks = kStaticMaxChunks;
   a.topk_idx = out->topk_idx;  // results go straight to the caller's buffers
   a.topk_w = out->topk_w;

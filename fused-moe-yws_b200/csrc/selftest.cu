@@ -52,10 +52,127 @@ __global__ void __launch_bounds__(64) wait_timeout_selftest_kernel(uint64_t time
   __syncthreads();
 }
 
+// ---------------------------------------------------------------------------------------
+// Dense FP8 tensor-core rate: one CTA per SM issues `mmas` back-to-back
+// tcgen05.mma.kind::f8f6f4 M128 x N256 x K32 (the instruction shape of the throughput
+// GEMMs) from one thread, alternating between two 256-column TMEM accumulators, on
+// operands staged once in shared memory (pseudo-random E4M3 bytes, no NaN encodings).
+// Nothing but the tensor pipe is busy, so the rate is the FP8 dense peak the GEMMs can
+// reach at the clock the GPU runs at.
+constexpr int kProbeThreads = 128;
+constexpr int kProbeABytes = 128 * 128;  // 128 rows x 128 B (K = 128, SWIZZLE_128B)
+constexpr int kProbeBBytes = 256 * 128;
+// 120 KB keeps a second probe CTA off the SM, so each CTA owns the whole TMEM
+constexpr int kProbeSmem = 120 * 1024;
+
+__global__ void __launch_bounds__(kProbeThreads, 1) fp8_mma_rate_kernel(int64_t mmas,
+                                                                        int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  __shared__ uint64_t done;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  const int warp = threadIdx.x >> 5;
+  for (int i = threadIdx.x; i < (kProbeABytes + kProbeBBytes) / 4; i += kProbeThreads) {
+    uint32_t x = (uint32_t)i * 2654435761u ^ (blockIdx.x * 40503u + 0x9E3779B9u);
+    x ^= x >> 15;
+    x *= 2246822519u;
+    x ^= x >> 13;
+    // clear bit 6 of every byte: no E4M3 NaN (0x7F / 0xFF), magnitudes below 2^-1
+    reinterpret_cast<uint32_t*>(smem)[i] = x & 0xBFBFBFBFu;
+  }
+  fence_proxy_async_smem();
+  if (threadIdx.x == 0) {
+    mbar_init(&done, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  if (threadIdx.x == 0) {
+    const uint32_t idesc = idesc_e4m3_f32(128, 256);
+    const uint64_t ad = smem_desc_kmajor(smem_addr(smem), 128);
+    const uint64_t bd = smem_desc_kmajor(smem_addr(smem + kProbeABytes), 128);
+    for (int64_t i = 0; i < mmas; ++i) {
+      const int sub = (int)(i & 3);
+      mma_f8f6f4(tmem + (uint32_t)((i >> 2) & 1) * 256, ad + 2 * sub, bd + 2 * sub, idesc,
+                 i >= 8 ? 1u : (sub > 0 ? 1u : 0u));
+    }
+    tc_commit(&done);
+    if (!mbar_wait(&done, 0, &abort_flag)) atomicOr(err, kErrTimeoutMma);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 }  // namespace
 }  // namespace fmoe
 
 using namespace fmoe;
+
+extern "C" int fmoe_probe_fp8_mma_rate(int64_t mmas_per_cta, double* tflops, double* ms,
+                                       void* stream_ptr) {
+  if (!tflops || !ms) {
+    set_last_error("tflops / ms must not be NULL");
+    return FMOE_ERR_VALUE;
+  }
+  if (mmas_per_cta < 64 || mmas_per_cta > (int64_t)1 << 22) {
+    set_last_error("mmas_per_cta must be in [64, 2^22]");
+    return FMOE_ERR_VALUE;
+  }
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(fp8_mma_rate_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kProbeSmem);
+  int* err = nullptr;
+  cudaEvent_t ev[2] = {nullptr, nullptr};
+  if (e == cudaSuccess) e = cudaMallocAsync(reinterpret_cast<void**>(&err), sizeof(int), stream);
+  if (e == cudaSuccess) e = cudaMemsetAsync(err, 0, sizeof(int), stream);
+  if (e == cudaSuccess) e = cudaEventCreate(&ev[0]);
+  if (e == cudaSuccess) e = cudaEventCreate(&ev[1]);
+  // one untimed launch (clocks ramp, code loads), then the timed one
+  for (int rep = 0; rep < 2 && e == cudaSuccess; ++rep) {
+    if (rep == 1) e = cudaEventRecord(ev[0], stream);
+    if (e == cudaSuccess) {
+      fp8_mma_rate_kernel<<<sms, kProbeThreads, kProbeSmem, stream>>>(mmas_per_cta, err);
+      e = cudaGetLastError();
+    }
+    if (rep == 1 && e == cudaSuccess) e = cudaEventRecord(ev[1], stream);
+  }
+  int herr = 0;
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  float t = 0.0f;
+  if (e == cudaSuccess) e = cudaEventElapsedTime(&t, ev[0], ev[1]);
+  if (err) cudaFreeAsync(err, stream);
+  for (cudaEvent_t x : ev)
+    if (x) cudaEventDestroy(x);
+  if (e != cudaSuccess) {
+    set_last_error(std::string("fp8 rate probe: ") + cudaGetErrorString(e));
+    return FMOE_ERR_RUNTIME;
+  }
+  if (herr != 0) {
+    set_last_error("fp8 rate probe: the completion wait timed out");
+    return FMOE_ERR_DEVICE;
+  }
+  *ms = t;
+  *tflops = (double)sms * (double)mmas_per_cta * (2.0 * 128 * 256 * 32) / (t * 1e-3) / 1e12;
+  return FMOE_OK;
+}
 
 extern "C" int fmoe_selftest_wait_timeout(uint64_t timeout_ns, uint64_t* result,
                                           void* stream_ptr) {

@@ -9,6 +9,14 @@
 // on the environment stream. Unlike the reference (kernel.cu:1834) it does not
 // synchronise the stream before returning.
 //
+// Device-side failures (a bounded wait inside a GEMM that ran out) cannot be seen when an
+// asynchronous call returns. Each call's last kernel reports its device error word to a
+// host-mapped word of the library, and every call starts by polling it
+// (fmoe_poll_device_error): a failure of an earlier call on the device raises RuntimeError
+// at the next call, as the reference's CHECK_CUDA (kernel.cu:53-62) raises on CUDA errors.
+// With FMOE_SYNC_CHECK=1 in the environment the call also synchronises the stream before
+// returning, like the reference, and raises for its own failure.
+//
 // Geometry is derived from the tensor shapes rather than hard-coded (kernel.cu:32-40):
 // E_global from routing_logits, E_local / 2I / H from gemm1_weights. n_group, topk_group
 // and top_k come from the definition table keyed by E_global (256 -> 8/4/8 for
@@ -19,6 +27,9 @@
 #include <tvm/ffi/extra/c_env_api.h>
 #include <tvm/ffi/function.h>
 
+#include <cuda_runtime.h>
+
+#include <cstdlib>
 #include <string>
 
 #include "fmoe.h"
@@ -52,6 +63,39 @@ void CheckSameDevice(const ffi::TensorView& a, const ffi::TensorView& b, const c
   if (a.device().device_type != b.device().device_type ||
       a.device().device_id != b.device().device_id)
     TVM_FFI_THROW(ValueError) << an << " and " << bn << " must be on the same device";
+}
+
+// Makes the tensors' device current for the call and restores the caller's device after.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != dev && cudaSetDevice(dev) != cudaSuccess)
+      TVM_FFI_THROW(RuntimeError) << "cudaSetDevice(" << dev << ") failed";
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+bool SyncCheckEnabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("FMOE_SYNC_CHECK");
+    return e && e[0] == '1';
+  }();
+  return on;
+}
+
+// Raise RuntimeError if a call on the current device has reported a device error word.
+void ThrowIfDeviceError(const char* when) {
+  int32_t bits = 0;
+  if (fmoe_poll_device_error(&bits) != FMOE_OK)
+    TVM_FFI_THROW(RuntimeError) << fmoe_last_error();
+  if (bits != 0)
+    TVM_FFI_THROW(RuntimeError) << when << ": the fused MoE kernels reported device error 0x"
+                                << std::hex << bits
+                                << " (a bounded wait expired); that call's output is invalid";
 }
 
 void ThrowStatus(int rc) {
@@ -118,6 +162,8 @@ ffi::Tensor kernel(const ffi::TensorView& routing_logits, const ffi::TensorView&
   if (fmoe_validate(&p) != FMOE_OK) ThrowStatus(FMOE_ERR_VALUE);
 
   const DLDevice device = routing_logits.device();
+  DeviceGuard guard(device.device_id);
+  ThrowIfDeviceError("an earlier call on this device");
   void* stream = TVMFFIEnvGetStream(device.device_type, device.device_id);
   ffi::Tensor out = ffi::Tensor::FromEnvAlloc(TVMFFIEnvTensorAlloc, ffi::Shape({T, H}), bf16, device);
   if (T == 0) return out;
@@ -138,6 +184,11 @@ ffi::Tensor kernel(const ffi::TensorView& routing_logits, const ffi::TensorView&
   t.output = out.data_ptr();
   const int rc = fmoe_forward(&p, &t, ws.data_ptr(), ws_bytes, stream);
   if (rc != FMOE_OK) ThrowStatus(rc);
+  if (SyncCheckEnabled()) {
+    const cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) TVM_FFI_THROW(RuntimeError) << "CUDA error: " << cudaGetErrorString(e);
+    ThrowIfDeviceError("this call");
+  }
   return out;
 }
 

@@ -35,7 +35,8 @@ EXPORTED_SYMBOLS = ("fmoe_abi_version", "fmoe_last_error", "fmoe_validate", "fmo
                     "fmoe_forward_routed", "fmoe_selftest_wait_timeout", "fmoe_ep_plan",
                     "fmoe_ep_pack", "fmoe_ep_unpack", "fmoe_ep_combine", "fmoe_ep_ipc_alloc",
                     "fmoe_ep_ipc_open", "fmoe_ep_ipc_close", "fmoe_ep_ipc_free",
-                    "fmoe_ep_pack_p2p", "fmoe_ep_return_p2p")
+                    "fmoe_ep_pack_p2p", "fmoe_ep_return_p2p", "fmoe_poll_device_error",
+                    "fmoe_selftest_inject_device_error", "fmoe_probe_fp8_mma_rate")
 
 
 class FmoeProblem(ctypes.Structure):
@@ -112,6 +113,10 @@ def load_library(path: Path | str | None = None):
         lib.fmoe_ep_pack_p2p.argtypes = [vp, vp, vp, vp, vp, i64, i32, i32, i32, vp, vp, i64, vp,
                                          vp]
         lib.fmoe_ep_return_p2p.argtypes = [vp, i64, i32, i32, vp, vp, vp, i64, vp, vp]
+        lib.fmoe_poll_device_error.argtypes = [ctypes.POINTER(ctypes.c_int32)]
+        lib.fmoe_selftest_inject_device_error.argtypes = [ctypes.c_int32]
+        lib.fmoe_probe_fp8_mma_rate.argtypes = [i64, ctypes.POINTER(ctypes.c_double),
+                                                ctypes.POINTER(ctypes.c_double), vp]
         for name in EXPORTED_SYMBOLS:
             if not hasattr(lib, name):
                 raise RuntimeError(f"{p} does not export {name}")
@@ -128,6 +133,38 @@ def _raise(lib, rc: int, where: str):
     if rc == FMOE_ERR_TYPE:
         raise TypeError(text)
     raise RuntimeError(text)
+
+
+class DeviceError(RuntimeError):
+    """A kernel of an earlier (or, with ``check=True``, this) call reported a device error
+    word: a bounded wait inside a GEMM ran out, so that call's output is invalid."""
+
+
+def poll_device_error(device=None) -> int:
+    """Error bits reported by calls on ``device`` that finished since the last poll (0 =
+    none); does not synchronise (fmoe_poll_device_error)."""
+    lib = load_library()
+    bits = ctypes.c_int32(0)
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else device) \
+        if not isinstance(device, torch.device) else device
+    with torch.cuda.device(dev):
+        rc = lib.fmoe_poll_device_error(ctypes.byref(bits))
+    if rc != FMOE_OK:
+        _raise(lib, rc, "poll_device_error")
+    return int(bits.value)
+
+
+def _raise_device_error(dev, when: str):
+    bits = poll_device_error(dev)
+    if bits:
+        raise DeviceError(f"{when}: the fused MoE kernels on {dev} reported device error "
+                          f"0x{bits:x} (a bounded wait expired); that call's output is invalid")
+
+
+def inject_device_error(bits: int) -> None:
+    """Test hook: the next forward call on this thread reports ``bits`` as its device error
+    word (fmoe_selftest_inject_device_error); nothing faults or waits."""
+    load_library().fmoe_selftest_inject_device_error(int(bits))
 
 
 def make_problem(T, E, E_local, H, I, local_expert_offset=0, routed_scaling_factor=2.5,
@@ -223,13 +260,18 @@ def _validate(routing_logits, routing_bias, hidden_states, hidden_states_scale, 
 def kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
            gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset: int,
            routed_scaling_factor: float, *, out: torch.Tensor | None = None, tile_n: int = 0,
-           workspace: torch.Tensor | None = None, routing: tuple | None = None) -> torch.Tensor:
+           workspace: torch.Tensor | None = None, routing: tuple | None = None,
+           check: bool = False) -> torch.Tensor:
     """Fused FP8 block-scaled DeepSeek-V3 MoE layer; returns bf16 [T, H].
 
     Same positional signature as the reference ``kernel`` (kernel.cu:1727-1734). Extra
     keyword-only arguments: ``out`` (destination), ``tile_n`` (override the autotune
     table), ``workspace`` (caller scratch), ``routing`` ((n_group, topk_group, top_k)
-    override). Work is enqueued on the current torch stream; no host synchronisation.
+    override), ``check`` (synchronise the stream and raise ``DeviceError`` if this call's
+    kernels reported a device error, as the reference's final synchronisation would,
+    kernel.cu:1834). Work is enqueued on the current torch stream; without ``check`` there
+    is no host synchronisation, and a device error of an earlier call on the device raises
+    ``DeviceError`` (a ``RuntimeError``) at the start of the next call.
     """
     T, E, EL, H, I = _validate(routing_logits, routing_bias, hidden_states, hidden_states_scale,
                                gemm1_weights, gemm1_weights_scale, gemm2_weights,
@@ -242,6 +284,7 @@ def kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale, gem
     if rc != FMOE_OK:
         _raise(lib, rc, "kernel")
     dev = routing_logits.device
+    _raise_device_error(dev, "an earlier call on this device")
     if out is None:
         out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
     else:
@@ -262,13 +305,17 @@ def kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale, gem
                               workspace.numel(), stream)
     if rc != FMOE_OK:
         _raise(lib, rc, "kernel")
+    if check:
+        torch.cuda.current_stream(dev).synchronize()
+        _raise_device_error(dev, "this call")
     return out
 
 
 def forward_routed(topk_idx, topk_w, hidden_states, hidden_states_scale, gemm1_weights,
                    gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
                    local_expert_offset: int, num_experts: int = 256, *, out=None,
-                   tile_n: int = 0, n_group=None, topk_group=None) -> torch.Tensor:
+                   tile_n: int = 0, n_group=None, topk_group=None,
+                   check: bool = False) -> torch.Tensor:
     """The operator on precomputed routing (``topk_idx`` int32 / ``topk_w`` fp32 [T, K]).
 
     Returns per-token sums over the local experts [offset, offset + E_local) in bf16.
@@ -289,6 +336,7 @@ def forward_routed(topk_idx, topk_w, hidden_states, hidden_states_scale, gemm1_w
     prob = make_problem(T, num_experts, EL, H, I, local_expert_offset, 1.0,
                         n_group or ng, topk_group or kg, K, tile_n)
     dev = hidden_states.device
+    _raise_device_error(dev, "an earlier call on this device")
     if out is None:
         out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
     if T == 0:
@@ -304,6 +352,9 @@ def forward_routed(topk_idx, topk_w, hidden_states, hidden_states_scale, gemm1_w
                                      ctypes.byref(tens), ws.data_ptr(), ws.numel(), stream)
     if rc != FMOE_OK:
         _raise(lib, rc, "forward_routed")
+    if check:
+        torch.cuda.current_stream(dev).synchronize()
+        _raise_device_error(dev, "this call")
     return out
 
 
@@ -519,6 +570,20 @@ def selftest_wait_timeout(timeout_ns: int = 2_000_000, device=None) -> dict:
         _raise(lib, rc, "selftest_wait_timeout")
     return {"expired_mask": int(res[0]), "mbarrier_wait_ns": int(res[1]),
             "flag_wait_ns": int(res[2])}
+
+
+def probe_fp8_mma_rate(mmas_per_cta: int = 16384, device=None) -> dict:
+    """Measured dense FP8 tensor-core rate of the current GPU (fmoe_probe_fp8_mma_rate):
+    {"tflops": dense TFLOP/s, "ms": time of the timed launch}."""
+    lib = load_library()
+    tf, ms = ctypes.c_double(0.0), ctypes.c_double(0.0)
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+    with torch.cuda.device(dev):
+        rc = lib.fmoe_probe_fp8_mma_rate(int(mmas_per_cta), ctypes.byref(tf), ctypes.byref(ms),
+                                         torch.cuda.current_stream(dev).cuda_stream)
+    if rc != FMOE_OK:
+        _raise(lib, rc, "probe_fp8_mma_rate")
+    return {"tflops": tf.value, "ms": ms.value}
 
 
 def plan_view(prob: FmoeProblem, workspace: torch.Tensor) -> dict:

@@ -106,6 +106,10 @@ class ExpertParallelMoE:
         self._cap_tokens = 0
         self._flag = None
         self._err = None
+        self._timed = False
+        # filled by a timed forward on CUDA (see _local)
+        self.local_stage_ms = None
+        self.last_local_tokens = self.last_local_rows = self.last_local_active = 0
 
     # ---- default B200 implementations --------------------------------------------------
     def _route_gpu(self, logits, bias):
@@ -200,12 +204,32 @@ class ExpertParallelMoE:
         hs_r, sc_r, idx_r, w_r = fmoe_b200.ep_unpack(self._peers.recv[me], H, K, rows=R,
                                                      device=dev)
         mark()
-        part = self.local_fn(idx_r, w_r, hs_r, sc_r, self.local_offset)
+        part = self._local(idx_r, w_r, hs_r, sc_r)
         mark()
         fmoe_b200.ep_return_p2p(part.contiguous(), starts_t, self._peers, shift_ret_t, cap,
                                 self._err)
         self._barrier()
         return fmoe_b200.ep_combine(self._peers.back[me], pos, T, H)
+
+    def _local(self, idx_r, w_r, hs_r, sc_r):
+        """The rank's own experts on what it received. In a timed pass on CUDA with the
+        default kernels, also records the operator's stage times (route, permute, gemm1,
+        gemm2, combine) and the received tokens, routed rows and active experts."""
+        if not (self._timed and hs_r.device.type == "cuda" and self.local_fn == self._local_gpu):
+            return self.local_fn(idx_r, w_r, hs_r, sc_r, self.local_offset)
+        import fmoe_b200
+
+        lo, hi = self.local_offset, self.local_offset + self.e_per_rank
+        sel = idx_r[(idx_r >= lo) & (idx_r < hi)]
+        self.last_local_tokens = int(idx_r.shape[0])
+        self.last_local_rows = int(sel.numel())
+        self.last_local_active = int(torch.unique(sel).numel())
+        st = fmoe_b200.StageTimer()
+        with st:
+            part = self.local_fn(idx_r, w_r, hs_r, sc_r, self.local_offset)
+        torch.cuda.synchronize()
+        self.local_stage_ms = st.times_ms()
+        return part
 
     # ---- the layer -------------------------------------------------------------------------
     def forward(self, routing_logits, routing_bias, hidden_states, hidden_states_scale,
@@ -214,6 +238,7 @@ class ExpertParallelMoE:
         K = self.top_k
         dev = hidden_states.device
         ev = []
+        self._timed = timed
 
         def mark():
             if timed and dev.type == "cuda":
@@ -272,7 +297,7 @@ class ExpertParallelMoE:
         else:
             hs_r, sc_r, idx_r, w_r = unpack_rows(recv, H, K)
         mark()
-        part = self.local_fn(idx_r, w_r, hs_r, sc_r, self.local_offset)
+        part = self._local(idx_r, w_r, hs_r, sc_r)
         mark()
         back = torch.empty(sum(send_splits), H, dtype=torch.bfloat16, device=dev)
         if self.world > 1:

@@ -122,6 +122,24 @@ int fmoe_route(const fmoe_problem* p, const float* routing_logits, const void* r
 int fmoe_read_device_error(const fmoe_problem* p, void* workspace, void* stream,
                            int32_t* device_error);
 
+/* Device errors without a synchronisation. The last kernel of every fmoe_forward() /
+ * fmoe_forward_routed() passes a non-zero device error word of its call (a bounded wait
+ * that ran out: that call's output is invalid) to a host-mapped word of the library, one
+ * per device. This reads it for the current device: *device_error = the error bits
+ * reported by calls that finished since the previous poll (0: none), without waiting for
+ * calls still running. The reference raises RuntimeError for every CUDA error
+ * (kernel.cu:53-62) after a full stream synchronisation (kernel.cu:1834); the TVM-FFI
+ * binding and the Python mirror poll at the start of every call and raise then. The word
+ * is allocated (8 bytes of pinned host memory) by a device's first call or poll that is not
+ * inside a stream capture; calls captured into a graph before that report nothing. */
+int fmoe_poll_device_error(int32_t* device_error);
+
+/* Test hook for the error path above (no fault, no hang): the next fmoe_forward() or
+ * fmoe_forward_routed() on the calling thread runs eagerly and its routing kernel ORs
+ * `bits` into the call's device error word, as an expired wait would; the call's output is
+ * still computed normally. The reference has no such hook. */
+int fmoe_selftest_inject_device_error(int32_t bits);
+
 /* Stage timing: when `events` is non-NULL, every later fmoe_forward() on this thread
  * records events[0..5] (cudaEvent_t handles owned by the caller) on its stream at the
  * stage boundaries: start, after routing, after permute/gather, after GEMM1+SwiGLU,
@@ -137,6 +155,14 @@ int fmoe_set_stage_events(void* const* events);
  * Synchronises `stream`, then writes result[0] = bitmask of the waits that expired
  * (bit 0 mbarrier, bit 1 flag; 3 when the limits work), result[1..2] = ns each waited. */
 int fmoe_selftest_wait_timeout(uint64_t timeout_ns, uint64_t* result, void* stream);
+
+/* Dense FP8 tensor-core rate of the current GPU, measured (no counterpart in the
+ * reference, which quotes no peak): one CTA per SM issues mmas_per_cta back-to-back
+ * tcgen05.mma.kind::f8f6f4 M128 x N256 x K32 instructions (the throughput GEMMs'
+ * instruction shape) on operands resident in shared memory; one untimed launch, then one
+ * timed with events on `stream`, which is synchronised. Writes *tflops (dense, 2 FLOP per
+ * multiply-add) and *ms. mmas_per_cta in [64, 2^22]; 16384 takes about 1 ms. */
+int fmoe_probe_fp8_mma_rate(int64_t mmas_per_cta, double* tflops, double* ms, void* stream);
 
 /* Debug view of the permutation of the last call (device pointers into the workspace):
  * expert counts [E_local], expert offsets [E_local+1], row->token [row_cap],
@@ -163,6 +189,9 @@ int fmoe_plan_view_get(const fmoe_problem* p, void* workspace, fmoe_plan_view* v
  * array: calls that overlap on the GPU race and must be ordered by the caller. */
 int fmoe_route_static(const fmoe_problem* p, const float* routing_logits,
                       const void* routing_bias, const fmoe_route_out* out, void* stream);
+/* (fmoe_route_static reports no device error word: within its limits the routing plan
+ * cannot overflow, which is the routing kernel's only device-side error. Its array's
+ * address is looked up again when the device's context changes, e.g. after a reset.) */
 
 /* Expert-parallel exchange, device side. The reference operator computes one expert slice
  * (local_expert_offset, kernel.cu:540-544) and leaves the exchange of tokens and partial

@@ -36,7 +36,11 @@ def _route_static(fmoe, prob, logits, bias, idx, w):
                                  ctypes.byref(out), stream)
 
 
-@pytest.mark.parametrize("E,E_local,T1,T2", [(256, 32, 64, 4096), (16, 16, 7, 100)])
+# (E_global, E_local, first call's tokens, second call's tokens). The largest case fills the
+# whole static scratch (8192 tokens: 512 CTAs x 64 experts of per-CTA counts and bases) and
+# is followed by a small one, so stale entries from the large call would show up.
+@pytest.mark.parametrize("E,E_local,T1,T2", [(256, 32, 64, 4096), (16, 16, 7, 100),
+                                             (256, 64, 8192, 64), (256, 64, 8192, 8192)])
 def test_route_static_matches_route_twice(fmoe, E, E_local, T1, T2):
     for call, T in enumerate((T1, T2)):
         logits, bias = _inputs(T, E, seed=40 + call)
@@ -47,7 +51,8 @@ def test_route_static_matches_route_twice(fmoe, E, E_local, T1, T2):
         rc = _route_static(fmoe, prob, logits, bias, idx, w)
         assert rc == fmoe.FMOE_OK, fmoe.load_library().fmoe_last_error()
         ref_idx, ref_w = fmoe.route(logits, bias, prob.n_group, prob.topk_group, prob.top_k,
-                                    prob.routed_scaling_factor, num_local_experts=E_local)
+                                    prob.routed_scaling_factor, num_local_experts=E_local,
+                                    local_expert_offset=prob.local_expert_offset)
         torch.cuda.synchronize()
         assert torch.equal(idx, ref_idx)
         assert np.array_equal(w.cpu().numpy().view(np.uint32),
@@ -63,3 +68,14 @@ def test_route_static_rejects_oversized(fmoe):
     rc = _route_static(fmoe, prob, logits, bias, idx, w)
     assert rc == fmoe.FMOE_ERR_VALUE
     assert b"exceeds the static scratch limit" in fmoe.load_library().fmoe_last_error()
+
+
+def test_route_static_rejects_too_many_local_experts(fmoe):
+    T = 64
+    logits, bias = _inputs(T, 256, seed=2)
+    prob = fmoe.make_problem(T, 256, 65, 7168, 2048)
+    idx = torch.empty(T, 8, dtype=torch.int32, device="cuda")
+    w = torch.empty(T, 8, dtype=torch.float32, device="cuda")
+    rc = _route_static(fmoe, prob, logits, bias, idx, w)
+    assert rc == fmoe.FMOE_ERR_VALUE
+    assert b"beyond the static limits" in fmoe.load_library().fmoe_last_error()
