@@ -159,9 +159,10 @@ __global__ void __launch_bounds__(kTmThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(mma_done + 2);
   volatile int* last_flag = abort_flag + 1;
-  // segment descriptors {tile, k0, k1, -} beside the 2-slot weight-scale ring: the producer
-  // walks the schedule and publishes each segment with its scales (tile < 0: no more work),
-  // so the epilogue warps hold no schedule state in registers
+  // segment descriptors {tile, k0 | k1 << 8, chunk row0, chunk rows} beside the 2-slot
+  // weight-scale ring: the producer walks the schedule and publishes each segment with its
+  // scales (tile < 0: no more work), so the epilogue warps hold no schedule state in
+  // registers and read no chunk record from global memory at the end of a tile
   int4* segd = reinterpret_cast<int4*>(mma_done + 4);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -254,7 +255,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
           dst[i] = __ldg(g + i);
           dst[kMaxKSteps + i] = __ldg(u + i);
         }
-        if (lane == 0) segd[ws] = make_int4(tile, k0, k1, 0);
+        if (lane == 0) segd[ws] = make_int4(tile, k0 | (k1 << 8), ch.row0, ch.rows);
         mbar_arrive(&wfull[ws]);  // every lane: its stores are released by its own arrive
         ++wseg;
       }
@@ -384,13 +385,18 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         ok = have;
         break;
       }
-      int k0, k1;
+      int k0, k1, row0, rows;
       {
         const int4 d = segd[ws];
         if (d.x < 0) break;  // no more work
-        k0 = d.y;
-        k1 = d.z;
+        k0 = d.y & 0xff;
+        k1 = d.y >> 8;
+        row0 = d.z;
+        rows = d.w;
       }
+      // GEMM2's routing weight of this thread's row, loaded now: its latency is hidden by the
+      // K loop instead of stalling the tile's finalize
+      const float w_row = !kG1 && row < rows ? __ldg(args.row_w + row0 + row) : 0.0f;
       const float* wrow = wsc + ws * 2 * kMaxKSteps;
 #pragma unroll
       for (int i = 0; i < NA; ++i) acc[i] = 0.0f;
@@ -462,7 +468,6 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       }
       const Schedule sched(num_tiles, KS, (int)gridDim.x, cta);
       const SplitRole role = split_role(sched, tile, k0, k1);
-      const Chunk ch = args.chunks[tile / args.m_tiles];
       const int m = tile % args.m_tiles;
       // ---- stream-K partial tiles ([row][256] fp32), finished by the last contributor ----
       if (role.split && role.pair) {
@@ -512,8 +517,8 @@ __global__ void __launch_bounds__(kTmThreads, 1)
         }
       }
 
-      const bool real = row < ch.rows;  // rows past the chunk belong to the next expert
-      const int64_t grow = (int64_t)ch.row0 + row;
+      const bool real = row < rows;  // rows past the chunk belong to the next expert
+      const int64_t grow = (int64_t)row0 + row;
       if constexpr (kG1) {
         // ---- SwiGLU, then FP8 hi/lo on one per-(token, 128-column) scale ----
         float amax = 0.0f;
@@ -566,7 +571,7 @@ __global__ void __launch_bounds__(kTmThreads, 1)
       } else {
         // ---- weighted expert output: 128 consecutive bf16 of this token row ----
         if (real) {
-          const float w = __ldg(args.row_w + grow);
+          const float w = w_row;
           // 32-byte stores: full sectors (H is a multiple of 256 on this path)
           __nv_bfloat16* dst = args.ow + grow * args.H + m * 256 + 128 * j;
 #pragma unroll

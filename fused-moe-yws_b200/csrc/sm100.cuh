@@ -250,6 +250,20 @@ __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// tcgen05.wait::ld, then an empty asm that redefines every register the preceding loads
+// wrote: asm volatile statements keep their order, so no use of those registers can be
+// scheduled above the wait.
+template <int N>
+__device__ __forceinline__ void tmem_ld_wait_tied(uint32_t (&r)[N]) {
+  static_assert(N % 8 == 0, "registers are tied 8 at a time");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < N; i += 8)
+    asm volatile(""
+                 : "+r"(r[i]), "+r"(r[i + 1]), "+r"(r[i + 2]), "+r"(r[i + 3]), "+r"(r[i + 4]),
+                   "+r"(r[i + 5]), "+r"(r[i + 6]), "+r"(r[i + 7]));
+}
+
 // 32-byte global store (one full sector per lane); p must be 32-byte aligned.
 __device__ __forceinline__ void st_global_v8(void* p, const uint32_t (&v)[8]) {
   asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v[0]),
