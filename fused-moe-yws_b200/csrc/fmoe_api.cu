@@ -234,14 +234,6 @@ RouteArgs route_args(const fmoe_problem* p, const Carved& c, const float* logits
   a.in_idx = nullptr;
   a.in_w = nullptr;
   a.inject_err = 0;
-  a.dense = 0;
-  a.hidden_scale = nullptr;
-  a.H = p->hidden_size;
-  a.token_row = c.at<int>(c.L.token_row);
-  a.row_w = c.at<float>(c.L.row_w);
-  a.row_token = c.at<int>(c.L.row_token);
-  a.a_scale = c.at<float>(c.L.a_scale);
-  a.tile_counters = c.at<int>(c.L.counters);
   a.logits = logits;
   a.bias = static_cast<const uint16_t*>(bias);
   a.T = p->num_tokens;
@@ -270,19 +262,14 @@ RouteArgs route_args(const fmoe_problem* p, const Carved& c, const float* logits
 
 int launch_route(const fmoe_problem* p, const Carved& c, const float* logits, const void* bias,
                  int bn, cudaStream_t stream, const int* in_idx = nullptr,
-                 const float* in_w = nullptr, int inject_err = 0,
-                 const float* dense_hidden_scale = nullptr) {
-  // meta words and the stream-K counters are contiguous: one small memset per call. The
-  // dense plan's routing kernel (one CTA, no last-CTA ticket) clears them itself.
-  if (!dense_hidden_scale)
-    FMOE_CUDA_TRY(cudaMemsetAsync(c.at<int>(c.L.meta), 0, c.L.counters - c.L.meta +
-                                  kTileCounters * sizeof(int), stream));
+                 const float* in_w = nullptr, int inject_err = 0) {
+  // meta words and the stream-K counters are contiguous: one small memset per call
+  FMOE_CUDA_TRY(cudaMemsetAsync(c.at<int>(c.L.meta), 0, c.L.counters - c.L.meta +
+                                kTileCounters * sizeof(int), stream));
   RouteArgs ra = route_args(p, c, logits, bias, bn);
   ra.in_idx = in_idx;
   ra.in_w = in_w;
   ra.inject_err = inject_err;
-  ra.dense = dense_hidden_scale != nullptr;
-  ra.hidden_scale = dense_hidden_scale;
   FMOE_CUDA_TRY(launch_pdl(route_plan_kernel, dim3((unsigned)c.L.n_route_ctas),
                            dim3(kRouteTokensPerCta * 32), 0, stream, ra));
   return FMOE_OK;
@@ -342,11 +329,6 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   const bool tm = bn == 128;  // throughput family: token rows on the MMA M side
   const int64_t T = p->num_tokens;
   const int H = p->hidden_size, I = p->intermediate_size, EL = p->num_local_experts;
-  // Dense decode plan: at most 16 tokens, routed here, 16-token chunks of the decode family.
-  // Every active expert's chunk covers all T tokens (token t = column t, the MMA's N = 16
-  // costs the same either way), so GEMM1 reads the token rows straight from hidden_states
-  // and the permute kernel -- and the workspace memset -- drop out of the call.
-  const bool dense = !in_idx && T <= kRouteTokensPerCta && bn == kRowAlign;
 
   int dev = 0;
   FMOE_CUDA_TRY(cudaGetDevice(&dev));
@@ -354,8 +336,7 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   const int inject = g_inject_err;
   g_inject_err = 0;
   if ((v = mark_stage(0, stream)) != FMOE_OK) return v;
-  v = launch_route(p, c, t->routing_logits, t->routing_bias, bn, stream, in_idx, in_w, inject,
-                   dense ? t->hidden_states_scale : nullptr);
+  v = launch_route(p, c, t->routing_logits, t->routing_bias, bn, stream, in_idx, in_w, inject);
   if (v != FMOE_OK) return v;
   if ((v = mark_stage(1, stream)) != FMOE_OK) return v;
 
@@ -379,7 +360,7 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   sa.a_perm = c.at<uint8_t>(c.L.a_perm);
   sa.a_scale = c.at<float>(c.L.a_scale);
   sa.meta = c.at<int>(c.L.meta);
-  if (!dense) {
+  {
     // split each row's columns over enough CTAs to cover the SMs at small T
     const int sms = num_sms_current();
     int parts = (int)((2 * sms + c.L.n_route_ctas - 1) / c.L.n_route_ctas);
@@ -396,10 +377,8 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   // token tiles of one C block as {byte in block, row, 128-byte block} with box {128, BN, 2}.
   CUtensorMap m_w13, m_a, m_w2, m_cq;
   uint8_t* cq = c.at<uint8_t>(c.L.cq);
-  if ((v = dense ? make_map(&m_a, t->hidden_states, H, (uint64_t)T, H, 128, bn,
-                            CU_TENSOR_MAP_SWIZZLE_128B, "hidden_states")
-                 : make_map(&m_a, sa.a_perm, H, c.L.row_cap, H, 128, bn,
-                            CU_TENSOR_MAP_SWIZZLE_128B, "permuted activations")) != FMOE_OK)
+  if ((v = make_map(&m_a, sa.a_perm, H, c.L.row_cap, H, 128, bn, CU_TENSOR_MAP_SWIZZLE_128B,
+                    "permuted activations")) != FMOE_OK)
     return v;
   if (tm) {
     if ((v = make_map(&m_w13, t->gemm1_weights, H, (uint64_t)EL * 2 * I, H, 128, 128,
@@ -441,7 +420,6 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   g.row_w = c.at<float>(c.L.row_w);
   g.ow = c.at<__nv_bfloat16>(c.L.ow);
   g.err = c.at<int>(c.L.meta) + kMetaError;
-  g.dense = dense;
   g.partials = c.at<float>(c.L.partials);
   g.tile_counters = c.at<int>(c.L.counters);
   const int sms = num_sms_current() < kMaxSms ? num_sms_current() : kMaxSms;

@@ -32,19 +32,6 @@ struct RouteArgs {
   int* meta;               // [kMetaWords]
   Chunk* chunks;           // [max_chunks]
   int inject_err;          // test hook: DeviceError bits CTA 0 ORs into the error word (0: none)
-  // Dense decode plan (T <= 16, one CTA, routing computed here): active expert j owns rows
-  // [16 j, 16 j + 16) and token t is row 16 j + t, so GEMM1 reads token rows straight from
-  // hidden_states and no permute kernel runs. The kernel then also writes token_row, row_w,
-  // row_token and the 16 token scale columns of a_scale, and zeroes the error word and the
-  // stream-K counters (no workspace memset precedes it).
-  int dense;
-  const float* hidden_scale;  // [H/128, T]
-  int H;
-  int* token_row;          // [T, K]
-  float* row_w;            // [row_cap]
-  int* row_token;          // [row_cap]
-  float* a_scale;          // [H/128, row_cap]
-  int* tile_counters;      // [kTileCounters]
 };
 
 struct ScatterArgs {
@@ -83,7 +70,6 @@ struct GemmArgs {
   const float* row_w;      // [row_cap]
   __nv_bfloat16* ow;       // [row_cap, H] weighted expert outputs
   int* err;                // device error word
-  int dense;               // GEMM1 token rows and scales at row 0 for every chunk (dense plan)
   float* partials;         // stream-K partial tiles, [CTA][2 slots]
   int* tile_counters;      // stream-K arrival counters by first contributor CTA (self-resetting)
 };

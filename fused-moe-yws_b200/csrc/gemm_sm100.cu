@@ -278,10 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   // The producer warp waits for the previous kernel only once its first weight boxes are
   // in flight (below); every other warp waits here, before touching its outputs.
-  // the permute / GEMM1 outputs of the previous kernel are visible after the wait. On the
-  // dense plan GEMM1 directly follows the routing kernel, which may let this grid start
-  // before its chunk list is written, so the producer waits first there too.
-  if (warp != 0 || args.dense) pdl_wait();
+  if (warp != 0) pdl_wait();  // the permute / GEMM1 outputs of the previous kernel are visible
   pdl_trigger();  // let the next kernel's CTAs start their prologue as SMs free up
 
   const int num_tiles = args.meta[kMetaNumChunks] * args.m_tiles;
@@ -300,7 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // before griddepcontrol.wait, overlapping the pipeline's first HBM latency with the
     // previous kernel's tail; the token tiles and their scales follow after the wait.
     int it = 0, wseg = 0, pre = 0;
-    bool ok = true, waited = args.dense != 0;
+    bool ok = true, waited = false;
     Schedule sched(num_tiles, KS, (int)gridDim.x, cta);
     int tile, k0, k1;
     while (ok && sched.next(tile, k0, k1)) {
@@ -356,10 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         waited = true;
       }
       if (lane == 0) {
-        // GEMM1 on the dense plan: every chunk's token tile is rows 0..15 of hidden_states
-        // and of the 16 token-scale columns
-        const int arow = kG1 && args.dense ? 0 : ch.row0;
-        const float* asrc = args.act_scale + arow;
+        const float* asrc = args.act_scale + ch.row0;
         for (int ks = k0; ks < k1; ++ks, ++it) {
           const int s = it % S, slot = it % SR;
           if (!mbar_wait(&empty[s], ((it / S) & 1) ^ 1, abort_flag) ||
@@ -370,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sb = stages + s * C::kStageBytes + C::kABytes;
           if (it >= pre) load_weights(s, ks);
           if constexpr (kG1) {
-            tma_load_2d(sb, &tmB, &full[s], ks * 128, arow, pol_a);
+            tma_load_2d(sb, &tmB, &full[s], ks * 128, ch.row0, pol_a);
           } else {
             // {byte in block, row, 128-byte block} box {128, BN, 2}: hi, then lo
             tma_load_3d(sb, &tmB, &full[s], 0, ch.row0, 2 * ks, pol_a);

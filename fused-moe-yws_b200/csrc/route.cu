@@ -207,12 +207,6 @@ __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
   for (int i = threadIdx.x; i < a.E_local; i += blockDim.x) s_cnt[i] = 0;
   pdl_wait();
   pdl_trigger();
-  if (a.dense) {
-    // no workspace memset ran before this call: clear what must start at zero (after the
-    // dependency wait, so the previous call's kernels have finished with these words)
-    for (int i = threadIdx.x; i < kTileCounters; i += blockDim.x) a.tile_counters[i] = 0;
-    if (threadIdx.x == 0) a.meta[kMetaError] = 0;
-  }
   if (a.inject_err != 0 && blockIdx.x == 0 && threadIdx.x == 0)
     atomicOr(a.meta + kMetaError, a.inject_err);
   __syncthreads();
@@ -443,39 +437,7 @@ __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
       ch.row0 = s_off[e] + r;
       ch.rows = n - r < a.bn ? n - r : a.bn;
       ch.ncols = (ch.rows + kRowAlign - 1) / kRowAlign * kRowAlign;
-      if (a.dense) {  // every token is a column of every chunk
-        ch.rows = (int)a.T;
-        ch.ncols = kRowAlign;
-      }
       a.chunks[s_choff[e] + c] = ch;
-    }
-  }
-  if (a.dense) {
-    // rows of the dense plan: a slot's rows carry no weight unless their token routes to the
-    // slot's expert
-    const int nrows = s_off[a.E_local];
-    for (int r = threadIdx.x; r < nrows; r += blockDim.x) {
-      a.row_w[r] = 0.0f;
-      a.row_token[r] = -1;
-    }
-    __syncthreads();
-    for (int i = threadIdx.x; i < (int)a.T * K; i += blockDim.x) {
-      const int t = i / K;
-      const int e = a.topk_idx[i];
-      const int le = e - a.local_offset;
-      int row = -1;
-      if (e >= 0 && le >= 0 && le < a.E_local) {
-        row = s_off[le] + t;
-        a.row_w[row] = a.topk_w[i];
-        a.row_token[row] = t;
-      }
-      a.token_row[i] = row;
-    }
-    // the 16 token-scale columns GEMM1 reads for every chunk, zero past T
-    for (int i = threadIdx.x; i < (a.H / kBlock) * kRowAlign; i += blockDim.x) {
-      const int kb = i / kRowAlign, t = i % kRowAlign;
-      a.a_scale[(int64_t)kb * a.row_cap + t] =
-          t < a.T ? a.hidden_scale[(int64_t)kb * a.T + t] : 0.0f;
     }
   }
 }

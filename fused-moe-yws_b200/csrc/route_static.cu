@@ -140,14 +140,6 @@ extern "C" int fmoe_route_static(const fmoe_problem* p, const float* routing_log
   a.in_idx = nullptr;
   a.in_w = nullptr;
   a.inject_err = 0;
-  a.dense = 0;
-  a.hidden_scale = nullptr;
-  a.H = p->hidden_size;
-  a.token_row = nullptr;
-  a.row_w = nullptr;
-  a.row_token = nullptr;
-  a.a_scale = nullptr;
-  a.tile_counters = nullptr;
   a.logits = routing_logits;
   a.bias = static_cast<const uint16_t*>(routing_bias);
   a.T = p->num_tokens;

@@ -193,20 +193,9 @@ def test_plan_bitexact(fmoe, oracle_mod, T):
     assert np.array_equal(view["expert_cnt"].cpu().numpy(), plan["expert_cnt"])
     assert np.array_equal(view["expert_off"].cpu().numpy(), plan["expert_off"])
     total = plan["total"]
-    assert int(view["meta"][1]) == total
-    if T <= 16:
-        # dense decode plan: each active expert's 16-row segment (the same offsets) holds
-        # token t at row offset + t, so GEMM1 reads token rows straight from hidden_states
-        off = plan["expert_off"]
-        want = np.full((T, 8), -1, np.int32)
-        for t in range(T):
-            for k in range(8):
-                if 0 <= idx_o[t, k] < geo.num_local:
-                    want[t, k] = off[idx_o[t, k]] + t
-        assert np.array_equal(view["token_row"].cpu().numpy(), want.ravel())
-        return
     assert np.array_equal(view["row_token"].cpu().numpy()[:total], plan["row_token"][:total])
     assert np.array_equal(view["token_row"].cpu().numpy(), plan["token_row"].ravel())
+    assert int(view["meta"][1]) == total
 
 
 @pytest.mark.parametrize("T", [1, 5, 64, 300])
