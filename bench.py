@@ -458,7 +458,7 @@ def run_layer_single(args, peaks, flush):
         ms = time_graph(lambda: call(*a4), args.steps, args.warmup, flush)
         torch.cuda.synchronize()
     ms_per_step = sum(ms) / len(ms)
-    tile_n = fmoe_b200.load_library().fmoe_autotune_tile_n(T)
+    tile_n = fmoe_b200.tile_n(fmoe_b200.make_problem(T, 256, 256, H, I))
     g1, g2 = kernel_rooflines(rows, active, stage_ms, hbm, fp8, fp8_src, hbm_src, tile_n)
     g1["traffic"] = stored_traffic(f"gemm1_layer_T{T}")
     g1["traffic_source"] = "ncu dram__bytes_read.sum + dram__bytes_write.sum (profiles/)"
@@ -535,7 +535,7 @@ def run_ep(args, world, rank, local, peaks):
     dist.all_reduce(br, op=dist.ReduceOp.MAX)
     st = layer.local_stage_ms or [0.0] * 5
     rows, active = layer.last_local_rows, layer.last_local_active
-    tile_n = fmoe_b200.load_library().fmoe_autotune_tile_n(layer.last_local_tokens)
+    tile_n = fmoe_b200.tile_n(fmoe_b200.make_problem(layer.last_local_tokens, 256, per, H, I))
     g1, g2 = kernel_rooflines(rows, active, st, hbm, fp8, fp8_src, hbm_src, tile_n)
     g1["stage_us"] = dict(zip(fmoe_b200.StageTimer.STAGES, [round(x * 1e3, 1) for x in st]))
     g1["gemm2"] = g2
@@ -609,7 +609,7 @@ def sweep_ours(args, w32, peaks, flush):
             stage_ms, eager = time_stages(fn, 10, flush)
             ms = time_graph(fn, 10, 3, flush)
             t = statistics.median(ms)
-            tn = tile or lib.fmoe_autotune_tile_n(T)
+            tn = tile or fmoe_b200.tile_n(fmoe_b200.make_problem(T, 256, 32, H, I))
             g1, g2 = kernel_rooflines(rows, active, stage_ms, hbm, fp8, fp8_src, hbm_src, tn)
             lay = roofline("whole layer", layer_bytes(T, active), rows * FLOP_PER_ROW, t, hbm,
                            fp8, fp8_src, hbm_src)
@@ -748,7 +748,7 @@ def run_slice(args, peaks, flush):
     with ClockSampler(gpu_index_of(0)) as clk:
         ms = time_graph(fn, args.steps, args.warmup, flush)
     t = sum(ms) / len(ms)
-    tn = fmoe_b200.load_library().fmoe_autotune_tile_n(T)
+    tn = fmoe_b200.tile_n(fmoe_b200.make_problem(T, 256, 32, H, I))
     g1, g2 = kernel_rooflines(rows, active, stage_ms, hbm, fp8, fp8_src, hbm_src, tn)
     g1["gemm2"] = g2
     g1["traffic"] = stored_traffic(f"gemm1_T{T}" + (f"_hot{args.skew}" if args.skew else ""))

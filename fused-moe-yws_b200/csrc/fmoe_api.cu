@@ -96,7 +96,7 @@ int validate(const fmoe_problem* p) {
 }
 
 int tile_n_of(const fmoe_problem* p) {
-  return resolve_tile_n(p->tile_n, p->num_tokens, p->hidden_size);
+  return resolve_tile_n(p->tile_n, p->num_tokens, p->top_k, p->num_experts, p->hidden_size);
 }
 
 bool aligned(const void* ptr, size_t a) { return (reinterpret_cast<uintptr_t>(ptr) % a) == 0; }
@@ -288,7 +288,15 @@ extern "C" const char* fmoe_last_error(void) { return g_last_error.c_str(); }
 
 extern "C" int fmoe_validate(const fmoe_problem* p) { return validate(p); }
 
-extern "C" int fmoe_autotune_tile_n(int64_t num_tokens) { return autotune_tile_n(num_tokens); }
+extern "C" int fmoe_autotune_tile_n(int64_t num_tokens) {
+  return autotune_tile_n(num_tokens, 8, 256);  // DeepSeek-V3 routing: top_k 8 of 256
+}
+
+extern "C" int fmoe_tile_n(const fmoe_problem* p) {
+  const int v = validate(p);
+  if (v != FMOE_OK) return -v;
+  return tile_n_of(p);
+}
 
 extern "C" int fmoe_workspace_size(const fmoe_problem* p, size_t* bytes) {
   const int v = validate(p);

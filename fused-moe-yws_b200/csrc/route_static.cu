@@ -135,7 +135,8 @@ extern "C" int fmoe_route_static(const fmoe_problem* p, const float* routing_log
   cudaError_t e = cudaMemsetAsync(scratch + kOffMeta, 0, kMetaWords * sizeof(int), stream);
   if (e != cudaSuccess) return fail_static(FMOE_ERR_RUNTIME, cudaGetErrorString(e));
 
-  const int bn = resolve_tile_n(p->tile_n, p->num_tokens, p->hidden_size);
+  const int bn =
+      resolve_tile_n(p->tile_n, p->num_tokens, p->top_k, p->num_experts, p->hidden_size);
   RouteArgs a;
   a.in_idx = nullptr;
   a.in_w = nullptr;

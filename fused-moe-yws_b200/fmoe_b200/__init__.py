@@ -36,7 +36,8 @@ EXPORTED_SYMBOLS = ("fmoe_abi_version", "fmoe_last_error", "fmoe_validate", "fmo
                     "fmoe_ep_pack", "fmoe_ep_unpack", "fmoe_ep_combine", "fmoe_ep_ipc_alloc",
                     "fmoe_ep_ipc_open", "fmoe_ep_ipc_close", "fmoe_ep_ipc_free",
                     "fmoe_ep_pack_p2p", "fmoe_ep_return_p2p", "fmoe_poll_device_error",
-                    "fmoe_selftest_inject_device_error", "fmoe_probe_fp8_mma_rate")
+                    "fmoe_selftest_inject_device_error", "fmoe_probe_fp8_mma_rate",
+                    "fmoe_tile_n")
 
 
 class FmoeProblem(ctypes.Structure):
@@ -85,6 +86,7 @@ def load_library(path: Path | str | None = None):
         lib.fmoe_workspace_size.argtypes = [ctypes.POINTER(FmoeProblem),
                                             ctypes.POINTER(ctypes.c_size_t)]
         lib.fmoe_autotune_tile_n.argtypes = [ctypes.c_int64]
+        lib.fmoe_tile_n.argtypes = [ctypes.POINTER(FmoeProblem)]
         lib.fmoe_forward.argtypes = [ctypes.POINTER(FmoeProblem), ctypes.POINTER(FmoeTensors),
                                      ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
         lib.fmoe_route.argtypes = [ctypes.POINTER(FmoeProblem), ctypes.c_void_p, ctypes.c_void_p,
@@ -179,6 +181,15 @@ def make_problem(T, E, E_local, H, I, local_expert_offset=0, routed_scaling_fact
     return FmoeProblem(int(T), int(E), int(E_local), int(H), int(I), int(top_k), int(n_group),
                        int(topk_group), int(local_expert_offset), float(routed_scaling_factor),
                        int(tile_n))
+
+
+def tile_n(prob: FmoeProblem) -> int:
+    """Token tile a call with this problem uses (fmoe_tile_n)."""
+    lib = load_library()
+    v = lib.fmoe_tile_n(ctypes.byref(prob))
+    if v < 0:
+        _raise(lib, -v, "tile_n")
+    return v
 
 
 def workspace_bytes(prob: FmoeProblem) -> int:

@@ -90,8 +90,16 @@ int fmoe_validate(const fmoe_problem* p);
  * here the caller owns the workspace, so the library itself never allocates. */
 int fmoe_workspace_size(const fmoe_problem* p, size_t* bytes);
 
-/* Token tile (MMA N) the committed autotune table picks for num_tokens. */
+/* Token tile (MMA N) the committed autotune table picks for num_tokens tokens of
+ * DeepSeek-V3 routing (top_k 8 of 256 experts). The table is keyed by the expected routed
+ * rows per local expert, num_tokens * top_k / num_experts (the reference's fixed tiles and
+ * T <= 512 switch, kernel.cu:41-51, :1781, have no such key). */
 int fmoe_autotune_tile_n(int64_t num_tokens);
+
+/* Token tile a call with this problem uses (its tile_n, or the table's choice for its
+ * tokens, top_k and experts; 64 where 128 would not divide hidden_size), or the negated
+ * status code if the problem is invalid. */
+int fmoe_tile_n(const fmoe_problem* p);
 
 /* The whole operator: routing -> permute/gather -> GEMM1+SwiGLU -> GEMM2 -> combine,
  * writing bf16 [T, H] into t->output. Replaces kernel() at kernel.cu:1727-1837, minus its

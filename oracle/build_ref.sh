@@ -3,7 +3,8 @@
 # solution/cuda/kernel.cu) from its own source location into oracle/_ref/ref_kernel.so.
 #
 # TEST INFRASTRUCTURE ONLY: the result is used to pin the CPU oracle against the
-# reference itself on a B200 (tests/test_gpu_reference.py, tests/golden/make_ref_goldens.py)
+# reference itself on a B200 (tests/test_gpu_parity.py::test_oracle_pinned_to_reference_kernel,
+# tests/golden/make_ref_goldens.py)
 # and as the timed comparator of `bench.py --impl reference`. No reference source is
 # copied into this repository; the compiler reads it in place.
 #

@@ -81,6 +81,24 @@ def test_autotune_table(fmoe):
     tiles = [lib.fmoe_autotune_tile_n(t) for t in (1, 64, 256, 512, 2048, 4096, 8192)]
     assert all(t in (16, 32, 64, 128, 256) for t in tiles)
     assert tiles == sorted(tiles)
+    # DeepSeek-V3 routing: the bounds of 8 and 24 expected rows per local expert
+    assert [lib.fmoe_autotune_tile_n(t) for t in (256, 257, 768, 769)] == [16, 64, 64, 128]
+
+
+def test_tile_follows_rows_per_expert(fmoe):
+    """The table is keyed by T * top_k / E_global: the DS-V3 slice, the whole 256-expert
+    layer and the 16-expert geometry reach the same tile at the same rows per expert."""
+    dsv3 = [fmoe.tile_n(fmoe.make_problem(t, 256, e, 7168, 2048)) for t in (256, 257, 769)
+            for e in (32, 256)]
+    assert dsv3 == [16, 16, 64, 64, 128, 128]
+    # 16 experts, top_k 4: 8 rows per expert at 32 tokens, 24 at 96
+    tiny = [fmoe.tile_n(fmoe.make_problem(t, 16, 16, 256, 128)) for t in (32, 33, 96, 97)]
+    assert tiny == [16, 64, 64, 128]
+    # the throughput family needs hidden_size % 256 == 0; otherwise 64
+    assert fmoe.tile_n(fmoe.make_problem(97, 16, 16, 384, 128)) == 64
+    assert fmoe.tile_n(fmoe.make_problem(1, 256, 32, 7168, 2048, tile_n=32)) == 32
+    with pytest.raises(ValueError):
+        fmoe.tile_n(fmoe.make_problem(1, 256, 32, 100, 2048))
 
 
 def test_forward_rejects_null_and_empty_without_gpu(fmoe):
