@@ -593,8 +593,10 @@ def sweep_ours(args, w32, peaks, flush):
     lists the token tiles timed per case (0 = the autotune table); tiles above 16 are
     skipped below T = 64, and 128 below T = 512."""
     hbm, fp8, hbm_src, fp8_src = peaks
-    lib = fmoe_b200.load_library()
     wargs = [w32[k] for k in W.OPERATOR_ARGS[4:]]
+    # the same weights pre-laid-out (fmoe_prelayout_weights): each case is also timed on them
+    w13p, w2p = fmoe_b200.prelayout_weights(w32["gemm1_weights"], w32["gemm2_weights"])
+    pargs = [w13p, w32["gemm1_weights_scale"], w2p, w32["gemm2_weights_scale"]]
     tiles = tuple(int(x) for x in args.sweep_tiles.split(","))
     res = []
     for cfg, T, skew in sweep_cases(args):
@@ -609,6 +611,9 @@ def sweep_ours(args, w32, peaks, flush):
             stage_ms, eager = time_stages(fn, 10, flush)
             ms = time_graph(fn, 10, 3, flush)
             t = statistics.median(ms)
+            fnp = lambda: fmoe_b200.kernel(*a4, *pargs, 0, RSF, out=out, tile_n=tile,  # noqa
+                                           prelaid=True)
+            t_pre = statistics.median(time_graph(fnp, 10, 3, flush))
             tn = tile or fmoe_b200.tile_n(fmoe_b200.make_problem(T, 256, 32, H, I))
             g1, g2 = kernel_rooflines(rows, active, stage_ms, hbm, fp8, fp8_src, hbm_src, tn)
             lay = roofline("whole layer", layer_bytes(T, active), rows * FLOP_PER_ROW, t, hbm,
@@ -616,6 +621,7 @@ def sweep_ours(args, w32, peaks, flush):
             res.append({"config": cfg, "T": T, "skew_hot": skew, "rows": rows,
                         "active_experts": active, "tile_n": tn,
                         "us_per_call": round(t * 1e3, 1),
+                        "us_per_call_prelaid_weights": round(t_pre * 1e3, 1),
                         "us_per_call_eager": round(statistics.median(eager) * 1e3, 1),
                         "tokens_per_s": round(T / (t * 1e-3), 1),
                         "roofline": {k: lay[k] for k in ("bound", "achieved", "peak", "unit",

@@ -309,9 +309,12 @@ extern "C" int fmoe_workspace_size(const fmoe_problem* p, size_t* bytes) {
 namespace fmoe {
 namespace {
 int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_idx,
-                const float* in_w, void* workspace, size_t workspace_bytes, void* stream_ptr) {
+                const float* in_w, void* workspace, size_t workspace_bytes, void* stream_ptr,
+                bool prelaid) {
   int v = validate(p);
   if (v != FMOE_OK) return v;
+  if (prelaid && p->hidden_size % 256 != 0)
+    return fail(FMOE_ERR_VALUE, "pre-laid-out weights need hidden_size to be a multiple of 256");
   if (!t) return fail(FMOE_ERR_VALUE, "tensors must not be NULL");
   if (p->num_tokens == 0) return FMOE_OK;  // empty batch: nothing to write
   if (in_idx && (!in_w || !aligned(in_idx, 16) || !aligned(in_w, 16)))
@@ -428,6 +431,7 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   g.row_w = c.at<float>(c.L.row_w);
   g.ow = c.at<__nv_bfloat16>(c.L.ow);
   g.err = c.at<int>(c.L.meta) + kMetaError;
+  g.w_pre = prelaid ? static_cast<const uint8_t*>(t->gemm1_weights) : nullptr;
   g.partials = c.at<float>(c.L.partials);
   g.tile_counters = c.at<int>(c.L.counters);
   const int sms = num_sms_current() < kMaxSms ? num_sms_current() : kMaxSms;
@@ -447,6 +451,7 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   g.m_tiles = tm ? H / 256 : (H + 255) / 256;
   g.k_steps = I / kBlock;
   g.w_scale = t->gemm2_weights_scale;
+  g.w_pre = prelaid ? static_cast<const uint8_t*>(t->gemm2_weights) : nullptr;
   g.act_scale = g.c_scale;
   bound = c.L.max_chunks * (int64_t)g.m_tiles;
   const int grid2 = (int)(bound < sms ? bound : sms);
@@ -491,6 +496,7 @@ namespace {
 // captured, calls with stage events on, and FMOE_GRAPH_CACHE=0 run eagerly.
 struct GraphKey {
   fmoe_problem p;
+  int prelaid;
   fmoe_tensors t;
   const void* in_idx;
   const void* in_w;
@@ -538,16 +544,17 @@ cudaStream_t capture_stream(int device) {
 
 int forward_cached(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_idx,
                    const float* in_w, void* workspace, size_t workspace_bytes,
-                   void* stream_ptr) {
+                   void* stream_ptr, bool prelaid = false) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if (!graph_cache_enabled() || g_stage_on || g_inject_err != 0 || !p || !t ||
       p->num_tokens <= 0 ||
       cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone)
-    return run_forward(p, t, in_idx, in_w, workspace, workspace_bytes, stream_ptr);
+    return run_forward(p, t, in_idx, in_w, workspace, workspace_bytes, stream_ptr, prelaid);
   GraphKey key;
   std::memset(&key, 0, sizeof(key));  // padding bytes take part in the comparison
   key.p = *p;
+  key.prelaid = prelaid;
   key.t = *t;
   key.in_idx = in_idx;
   key.in_w = in_w;
@@ -578,16 +585,16 @@ int forward_cached(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* 
     }
     g_graphs.push_back(GraphEntry{key, nullptr, ++g_graph_clock});
     lock.unlock();
-    return run_forward(p, t, in_idx, in_w, workspace, workspace_bytes, stream_ptr);
+    return run_forward(p, t, in_idx, in_w, workspace, workspace_bytes, stream_ptr, prelaid);
   }
   // second sighting: capture on the library stream, then launch on the caller's stream
   cudaStream_t cs = capture_stream(key.device);
   if (!cs) {
     lock.unlock();
-    return run_forward(p, t, in_idx, in_w, workspace, workspace_bytes, stream_ptr);
+    return run_forward(p, t, in_idx, in_w, workspace, workspace_bytes, stream_ptr, prelaid);
   }
   FMOE_CUDA_TRY(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
-  const int v = run_forward(p, t, in_idx, in_w, workspace, workspace_bytes, cs);
+  const int v = run_forward(p, t, in_idx, in_w, workspace, workspace_bytes, cs, prelaid);
   cudaGraph_t graph = nullptr;
   const cudaError_t ec = cudaStreamEndCapture(cs, &graph);
   if (v != FMOE_OK) {
@@ -624,6 +631,49 @@ extern "C" int fmoe_forward_routed(const fmoe_problem* p, const int32_t* topk_id
                                    size_t workspace_bytes, void* stream_ptr) {
   if (!topk_idx || !topk_w) return fail(FMOE_ERR_VALUE, "topk_idx / topk_w must not be NULL");
   return forward_cached(p, t, topk_idx, topk_w, workspace, workspace_bytes, stream_ptr);
+}
+
+extern "C" int fmoe_forward_prelaid(const fmoe_problem* p, const fmoe_tensors* t,
+                                    void* workspace, size_t workspace_bytes, void* stream_ptr) {
+  return forward_cached(p, t, nullptr, nullptr, workspace, workspace_bytes, stream_ptr, true);
+}
+
+extern "C" int fmoe_forward_routed_prelaid(const fmoe_problem* p, const int32_t* topk_idx,
+                                           const float* topk_w, const fmoe_tensors* t,
+                                           void* workspace, size_t workspace_bytes,
+                                           void* stream_ptr) {
+  if (!topk_idx || !topk_w) return fail(FMOE_ERR_VALUE, "topk_idx / topk_w must not be NULL");
+  return forward_cached(p, t, topk_idx, topk_w, workspace, workspace_bytes, stream_ptr, true);
+}
+
+extern "C" int fmoe_prelayout_weights(const fmoe_problem* p, const void* gemm1_weights,
+                                      const void* gemm2_weights, void* gemm1_out,
+                                      void* gemm2_out, void* stream_ptr) {
+  int v = validate(p);
+  if (v != FMOE_OK) return v;
+  if (p->hidden_size % 256 != 0)
+    return fail(FMOE_ERR_VALUE, "pre-laid-out weights need hidden_size to be a multiple of 256");
+  if (!gemm1_weights || !gemm2_weights || !gemm1_out || !gemm2_out)
+    return fail(FMOE_ERR_VALUE, "weight pointers must not be NULL");
+  const void* ptrs[] = {gemm1_weights, gemm2_weights, gemm1_out, gemm2_out};
+  for (const void* q : ptrs)
+    if (!aligned(q, 16)) return fail(FMOE_ERR_VALUE, "weight pointers must be 16-byte aligned");
+  const size_t b1 = (size_t)p->num_local_experts * 2 * p->intermediate_size * p->hidden_size;
+  const size_t b2 = (size_t)p->num_local_experts * p->hidden_size * p->intermediate_size;
+  auto overlaps = [](const void* a, size_t na, const void* b, size_t nb) {
+    const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+    return x < y + nb && y < x + na;
+  };
+  if (overlaps(gemm1_out, b1, gemm1_weights, b1) || overlaps(gemm1_out, b1, gemm2_weights, b2) ||
+      overlaps(gemm2_out, b2, gemm1_weights, b1) || overlaps(gemm2_out, b2, gemm2_weights, b2) ||
+      overlaps(gemm1_out, b1, gemm2_out, b2))
+    return fail(FMOE_ERR_VALUE, "pre-layout outputs must not overlap the weights or each other");
+  FMOE_CUDA_TRY(launch_prelayout(static_cast<const uint8_t*>(gemm1_weights),
+                                 static_cast<const uint8_t*>(gemm2_weights),
+                                 static_cast<uint8_t*>(gemm1_out), static_cast<uint8_t*>(gemm2_out),
+                                 p->num_local_experts, p->hidden_size, p->intermediate_size,
+                                 static_cast<cudaStream_t>(stream_ptr)));
+  return FMOE_OK;
 }
 
 extern "C" int fmoe_set_stage_events(void* const* events) {

@@ -70,6 +70,10 @@ struct GemmArgs {
   const float* row_w;      // [row_cap]
   __nv_bfloat16* ow;       // [row_cap, H] weighted expert outputs
   int* err;                // device error word
+  // Weights laid out ahead of time (fmoe_prelayout_weights), or null: every K step's 32 KB
+  // weight tile of (expert, m tile) stored as the swizzled shared-memory image, tiles
+  // [expert][m tile][k step] back to back, so one contiguous bulk copy fetches it.
+  const uint8_t* w_pre;
   float* partials;         // stream-K partial tiles, [CTA][2 slots]
   int* tile_counters;      // stream-K arrival counters by first contributor CTA (self-resetting)
 };
@@ -133,6 +137,10 @@ cudaError_t launch_gemm1_tm(const CUtensorMap& a_map, const CUtensorMap& w13_map
 cudaError_t launch_gemm2_tm(const CUtensorMap& cq_map, const CUtensorMap& w2_map,
                             const GemmArgs& args, int grid, cudaStream_t stream);
 bool gemm_bn_supported(int bn);
+// Tile images of fmoe_prelayout_weights (gemm_sm100.cu).
+constexpr int kPrelaidTileBytes = 256 * 128;
+cudaError_t launch_prelayout(const uint8_t* w13, const uint8_t* w2, uint8_t* w13_out,
+                             uint8_t* w2_out, int E_local, int H, int I, cudaStream_t stream);
 void set_last_error(const std::string& msg);  // message returned by fmoe_last_error()
 size_t gemm_partial_bytes();
 

@@ -336,7 +336,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto load_weights = [&](int s, int ks) {
         uint8_t* sa = stages + s * C::kStageBytes;
         mbar_arrive_expect_tx(&full[s], C::kTx);
-        if constexpr (kG1) {
+        if (args.w_pre) {
+          // the same 32 KB image, stored contiguously ahead of time: one bulk copy
+          const int64_t t = ((int64_t)ch.expert * args.m_tiles + m) * KS + ks;
+          bulk_load_1d_hint(sa, args.w_pre + t * kPrelaidTileBytes, kPrelaidTileBytes, &full[s],
+                            pol_w);
+        } else if constexpr (kG1) {
           // {K, row in half, (expert, gate|up)} box {128, 128, 2}: gate tile, then up tile
           tma_load_3d(sa, &tmA, &full[s], ks * 128, m * 128, 2 * ch.expert, pol_w);
         } else {
@@ -653,7 +658,44 @@ cudaError_t launch_one(const CUtensorMap& a, const CUtensorMap& b, const GemmArg
   return launch_pdl(fn, dim3(grid), dim3(kThreads), C::kSmemBytes, stream, a, b, args);
 }
 
+// Weight pre-layout: every (expert, m tile, K step) weight tile the GEMMs load -- GEMM1:
+// gate rows [128 m, 128 m + 128) then up rows [I + 128 m, ...) of W13; GEMM2: rows
+// [256 m, 256 m + 256) of W2; 128 K bytes each -- written as the 32 KB shared-memory image a
+// SWIZZLE_128B tensor-map load produces (16-byte chunk c of row r at chunk c ^ (r % 8)),
+// tiles ordered [expert][m tile][K step]. One CTA per tile, one 16-byte chunk per thread
+// step; reads and writes are coalesced per 128-byte row.
+__global__ void __launch_bounds__(256) prelayout_kernel(const uint8_t* __restrict__ w,
+                                                        uint8_t* __restrict__ out, int rows,
+                                                        int cols, int m_tiles, int k_steps,
+                                                        int gemm1, int I) {
+  const int64_t tile = blockIdx.x;
+  const int ks = (int)(tile % k_steps);
+  const int m = (int)((tile / k_steps) % m_tiles);
+  const int64_t e = tile / ((int64_t)k_steps * m_tiles);
+  const uint8_t* src = w + e * (int64_t)rows * cols;
+  uint8_t* dst = out + tile * kPrelaidTileBytes;
+  for (int i = threadIdx.x; i < 256 * 8; i += blockDim.x) {
+    const int r = i >> 3, c = i & 7;
+    const int srow = gemm1 ? (r < 128 ? 128 * m + r : I + 128 * m + (r - 128)) : 256 * m + r;
+    const uint4 v =
+        *reinterpret_cast<const uint4*>(src + (int64_t)srow * cols + ks * 128 + c * 16);
+    *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) * 16)) = v;
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_prelayout(const uint8_t* w13, const uint8_t* w2, uint8_t* w13_out,
+                             uint8_t* w2_out, int E_local, int H, int I, cudaStream_t stream) {
+  const int64_t t1 = (int64_t)E_local * (I / 128) * (H / 128);
+  const int64_t t2 = (int64_t)E_local * (H / 256) * (I / 128);
+  prelayout_kernel<<<(unsigned)t1, 256, 0, stream>>>(w13, w13_out, 2 * I, H, I / 128, H / 128,
+                                                     1, I);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  prelayout_kernel<<<(unsigned)t2, 256, 0, stream>>>(w2, w2_out, H, I, H / 256, I / 128, 0, I);
+  return cudaGetLastError();
+}
 
 bool gemm_bn_supported(int bn) { return bn == 16 || bn == 32 || bn == 64 || bn == 128; }
 

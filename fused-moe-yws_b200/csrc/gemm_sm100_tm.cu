@@ -273,12 +273,20 @@ __global__ void __launch_bounds__(kTmThreads, 1)
           mbar_arrive_expect_tx(&full[s], C::kStageBytes);
           if constexpr (kG1) {
             tma_load_2d(sa, &tmA, &full[s], ks * 128, ch.row0, pol_a);
+          } else {
+            tma_load_2d(sa, &tmA, &full[s], ks * 256, ch.row0, pol_a);                    // hi
+            tma_load_2d(sa + 128 * 128, &tmA, &full[s], ks * 256 + 128, ch.row0, pol_a);  // lo
+          }
+          if (args.w_pre) {
+            // the weight tile's 32 KB image stored ahead of time: one contiguous bulk copy
+            const int64_t t = ((int64_t)ch.expert * args.m_tiles + m) * KS + ks;
+            bulk_load_1d_hint(sb, args.w_pre + t * kPrelaidTileBytes, kPrelaidTileBytes,
+                              &full[s], pol_w);
+          } else if constexpr (kG1) {
             const int wrow = ch.expert * 2 * args.I + m * 128;
             tma_load_2d(sb, &tmB, &full[s], ks * 128, wrow, pol_w);
             tma_load_2d(sb + 128 * 128, &tmB, &full[s], ks * 128, wrow + args.I, pol_w);
           } else {
-            tma_load_2d(sa, &tmA, &full[s], ks * 256, ch.row0, pol_a);                    // hi
-            tma_load_2d(sa + 128 * 128, &tmA, &full[s], ks * 256 + 128, ch.row0, pol_a);  // lo
             const int wrow = ch.expert * args.H + m * 256;
             tma_load_2d(sb, &tmB, &full[s], ks * 128, wrow, pol_w);
             tma_load_2d(sb + 128 * 128, &tmB, &full[s], ks * 128, wrow + 128, pol_w);

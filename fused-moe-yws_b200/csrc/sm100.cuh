@@ -135,6 +135,16 @@ __device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_
       : "memory");
 }
 
+// 1D bulk copy with an L2 eviction-priority policy (see policy_evict_* below).
+__device__ __forceinline__ void bulk_load_1d_hint(void* dst, const void* src, uint32_t bytes,
+                                                  uint64_t* bar, uint64_t cache_hint) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1], %2, [%3], %4;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar)), "l"(cache_hint)
+      : "memory");
+}
+
 // L2 eviction-priority policies for the cache_hint operand.
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
@@ -248,20 +258,6 @@ __device__ __forceinline__ void tmem_ld_32x32b<32>(uint32_t taddr, uint32_t (&r)
 
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-
-// tcgen05.wait::ld, then an empty asm that redefines every register the preceding loads
-// wrote: asm volatile statements keep their order, so no use of those registers can be
-// scheduled above the wait.
-template <int N>
-__device__ __forceinline__ void tmem_ld_wait_tied(uint32_t (&r)[N]) {
-  static_assert(N % 8 == 0, "registers are tied 8 at a time");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < N; i += 8)
-    asm volatile(""
-                 : "+r"(r[i]), "+r"(r[i + 1]), "+r"(r[i + 2]), "+r"(r[i + 3]), "+r"(r[i + 4]),
-                   "+r"(r[i + 5]), "+r"(r[i + 6]), "+r"(r[i + 7]));
 }
 
 // 32-byte global store (one full sector per lane); p must be 32-byte aligned.

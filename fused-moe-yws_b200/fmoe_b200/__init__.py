@@ -37,7 +37,8 @@ EXPORTED_SYMBOLS = ("fmoe_abi_version", "fmoe_last_error", "fmoe_validate", "fmo
                     "fmoe_ep_ipc_open", "fmoe_ep_ipc_close", "fmoe_ep_ipc_free",
                     "fmoe_ep_pack_p2p", "fmoe_ep_return_p2p", "fmoe_poll_device_error",
                     "fmoe_selftest_inject_device_error", "fmoe_probe_fp8_mma_rate",
-                    "fmoe_tile_n")
+                    "fmoe_tile_n", "fmoe_prelayout_weights", "fmoe_forward_prelaid",
+                    "fmoe_forward_routed_prelaid")
 
 
 class FmoeProblem(ctypes.Structure):
@@ -87,6 +88,9 @@ def load_library(path: Path | str | None = None):
                                             ctypes.POINTER(ctypes.c_size_t)]
         lib.fmoe_autotune_tile_n.argtypes = [ctypes.c_int64]
         lib.fmoe_tile_n.argtypes = [ctypes.POINTER(FmoeProblem)]
+        lib.fmoe_prelayout_weights.argtypes = [ctypes.POINTER(FmoeProblem), ctypes.c_void_p,
+                                               ctypes.c_void_p, ctypes.c_void_p,
+                                               ctypes.c_void_p, ctypes.c_void_p]
         lib.fmoe_forward.argtypes = [ctypes.POINTER(FmoeProblem), ctypes.POINTER(FmoeTensors),
                                      ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
         lib.fmoe_route.argtypes = [ctypes.POINTER(FmoeProblem), ctypes.c_void_p, ctypes.c_void_p,
@@ -103,6 +107,9 @@ def load_library(path: Path | str | None = None):
         lib.fmoe_forward_routed.argtypes = [ctypes.POINTER(FmoeProblem), ctypes.c_void_p,
                                             ctypes.c_void_p, ctypes.POINTER(FmoeTensors),
                                             ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+        # the prelaid entry points take the same arguments (assigned after their sources)
+        lib.fmoe_forward_prelaid.argtypes = lib.fmoe_forward.argtypes
+        lib.fmoe_forward_routed_prelaid.argtypes = lib.fmoe_forward_routed.argtypes
         vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
         lib.fmoe_ep_plan.argtypes = [vp, i64, i32, i32, i32, vp, vp, vp, vp]
         lib.fmoe_ep_pack.argtypes = [vp, vp, vp, vp, vp, i64, i32, i32, i32, vp, vp]
@@ -122,6 +129,10 @@ def load_library(path: Path | str | None = None):
         for name in EXPORTED_SYMBOLS:
             if not hasattr(lib, name):
                 raise RuntimeError(f"{p} does not export {name}")
+        for name in ("fmoe_forward", "fmoe_forward_routed", "fmoe_forward_prelaid",
+                     "fmoe_forward_routed_prelaid"):
+            if getattr(lib, name).argtypes is None:
+                raise RuntimeError(f"{name}: argument types not set")
         if path is None:
             _lib = lib
         return lib
@@ -272,7 +283,7 @@ def kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale, gem
            gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset: int,
            routed_scaling_factor: float, *, out: torch.Tensor | None = None, tile_n: int = 0,
            workspace: torch.Tensor | None = None, routing: tuple | None = None,
-           check: bool = False) -> torch.Tensor:
+           check: bool = False, prelaid: bool = False) -> torch.Tensor:
     """Fused FP8 block-scaled DeepSeek-V3 MoE layer; returns bf16 [T, H].
 
     Same positional signature as the reference ``kernel`` (kernel.cu:1727-1734). Extra
@@ -280,7 +291,8 @@ def kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale, gem
     table), ``workspace`` (caller scratch), ``routing`` ((n_group, topk_group, top_k)
     override), ``check`` (synchronise the stream and raise ``DeviceError`` if this call's
     kernels reported a device error, as the reference's final synchronisation would,
-    kernel.cu:1834). Work is enqueued on the current torch stream; without ``check`` there
+    kernel.cu:1834), ``prelaid`` (the weight tensors are ``prelayout_weights`` outputs).
+    Work is enqueued on the current torch stream; without ``check`` there
     is no host synchronisation, and a device error of an earlier call on the device raises
     ``DeviceError`` (a ``RuntimeError``) at the start of the next call.
     """
@@ -312,8 +324,9 @@ def kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale, gem
                        gemm2_weights.data_ptr(), gemm2_weights_scale.data_ptr(), out.data_ptr())
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev).cuda_stream
-        rc = lib.fmoe_forward(ctypes.byref(prob), ctypes.byref(tens), workspace.data_ptr(),
-                              workspace.numel(), stream)
+        fwd = lib.fmoe_forward_prelaid if prelaid else lib.fmoe_forward
+        rc = fwd(ctypes.byref(prob), ctypes.byref(tens), workspace.data_ptr(), workspace.numel(),
+                 stream)
     if rc != FMOE_OK:
         _raise(lib, rc, "kernel")
     if check:
@@ -326,7 +339,7 @@ def forward_routed(topk_idx, topk_w, hidden_states, hidden_states_scale, gemm1_w
                    gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
                    local_expert_offset: int, num_experts: int = 256, *, out=None,
                    tile_n: int = 0, n_group=None, topk_group=None,
-                   check: bool = False) -> torch.Tensor:
+                   check: bool = False, prelaid: bool = False) -> torch.Tensor:
     """The operator on precomputed routing (``topk_idx`` int32 / ``topk_w`` fp32 [T, K]).
 
     Returns per-token sums over the local experts [offset, offset + E_local) in bf16.
@@ -359,14 +372,38 @@ def forward_routed(topk_idx, topk_w, hidden_states, hidden_states_scale, gemm1_w
                        gemm2_weights.data_ptr(), gemm2_weights_scale.data_ptr(), out.data_ptr())
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev).cuda_stream
-        rc = lib.fmoe_forward_routed(ctypes.byref(prob), topk_idx.data_ptr(), topk_w.data_ptr(),
-                                     ctypes.byref(tens), ws.data_ptr(), ws.numel(), stream)
+        fwd = lib.fmoe_forward_routed_prelaid if prelaid else lib.fmoe_forward_routed
+        rc = fwd(ctypes.byref(prob), topk_idx.data_ptr(), topk_w.data_ptr(), ctypes.byref(tens),
+                 ws.data_ptr(), ws.numel(), stream)
     if rc != FMOE_OK:
         _raise(lib, rc, "forward_routed")
     if check:
         torch.cuda.current_stream(dev).synchronize()
         _raise_device_error(dev, "this call")
     return out
+
+
+def prelayout_weights(gemm1_weights: torch.Tensor, gemm2_weights: torch.Tensor):
+    """The weights as the GEMMs load them (fmoe_prelayout_weights): new tensors of the same
+    shapes and dtype holding every 128-K weight tile as its swizzled shared-memory image,
+    for ``kernel(..., prelaid=True)`` / ``forward_routed(..., prelaid=True)``. The FP8 values
+    and the scale tensors are unchanged; done once per set of weights, not per call."""
+    EL, two_i, H = gemm1_weights.shape
+    I = two_i // 2
+    _check_tensor(gemm1_weights, "gemm1_weights", (EL, 2 * I, H), _F8)
+    _check_tensor(gemm2_weights, "gemm2_weights", (EL, H, I), _F8)
+    lib = load_library()
+    prob = make_problem(1, 256, EL, H, I)
+    out1 = torch.empty_like(gemm1_weights)
+    out2 = torch.empty_like(gemm2_weights)
+    dev = gemm1_weights.device
+    with torch.cuda.device(dev):
+        rc = lib.fmoe_prelayout_weights(ctypes.byref(prob), gemm1_weights.data_ptr(),
+                                        gemm2_weights.data_ptr(), out1.data_ptr(),
+                                        out2.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
+    if rc != FMOE_OK:
+        _raise(lib, rc, "prelayout_weights")
+    return out1, out2
 
 
 def route(routing_logits: torch.Tensor, routing_bias: torch.Tensor, n_group: int,

@@ -118,6 +118,27 @@ int fmoe_forward_routed(const fmoe_problem* p, const int32_t* topk_idx, const fl
                         const fmoe_tensors* t, void* workspace, size_t workspace_bytes,
                         void* stream);
 
+/* Weight pre-layout (the weight side of the reference's per-call dequantise passes,
+ * kernel.cu:924-1003, done once instead): writes every 32 KB weight tile the GEMMs load per
+ * 128-K step -- GEMM1: 128 gate rows then the matching 128 up rows of W13; GEMM2: 256 rows
+ * of W2 -- as the swizzled shared-memory image the GEMMs consume, tiles ordered [expert]
+ * [row tile][K step], into gemm1_out / gemm2_out (each the size of its input, 16-byte
+ * aligned, not overlapping the inputs). The values are unchanged (FP8 bytes moved, scales
+ * untouched), so the prelaid entry points below give the same output bits, with each
+ * weight tile fetched by one contiguous bulk copy. Needs hidden_size % 256 == 0.
+ * Asynchronous on `stream`. */
+int fmoe_prelayout_weights(const fmoe_problem* p, const void* gemm1_weights,
+                           const void* gemm2_weights, void* gemm1_out, void* gemm2_out,
+                           void* stream);
+
+/* fmoe_forward / fmoe_forward_routed with t->gemm1_weights and t->gemm2_weights pointing at
+ * fmoe_prelayout_weights outputs (scales as usual). */
+int fmoe_forward_prelaid(const fmoe_problem* p, const fmoe_tensors* t, void* workspace,
+                         size_t workspace_bytes, void* stream);
+int fmoe_forward_routed_prelaid(const fmoe_problem* p, const int32_t* topk_idx,
+                                const float* topk_w, const fmoe_tensors* t, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
 /* Routing only (replaces sigmoid_bias_kernel + routing_select_kernel,
  * kernel.cu:388-516), for parity tests and the expert-parallel dispatch.
  * Needs the same workspace as fmoe_forward. */

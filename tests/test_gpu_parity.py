@@ -352,3 +352,66 @@ def test_library_graph_cache_replays_and_reads_current_inputs(fmoe, T):
     torch.cuda.synchronize()
     assert not torch.equal(out.view(torch.int16), ref.view(torch.int16))
     assert torch.equal(out.view(torch.int16), fresh.view(torch.int16))
+
+
+# ----------------------------------------------------------------------------- weight pre-layout
+def _prelayout_numpy(w13, w2, I):
+    """Restatement of fmoe_prelayout_weights: every (expert, row tile, 128-K step) weight tile
+    as 256 rows x 128 bytes with 16-byte chunk c of row r stored at chunk c ^ (r % 8)."""
+    E, _, H = w13.shape
+    tiles1, tiles2 = [], []
+    perm = np.array([[c ^ (r & 7) for c in range(8)] for r in range(256)])
+
+    def image(rows):  # rows: [256, 128] uint8
+        out = np.empty_like(rows)
+        for r in range(256):
+            chunks = rows[r].reshape(8, 16)
+            out[r].reshape(8, 16)[perm[r]] = chunks
+        return out
+
+    for e in range(E):
+        for m in range(I // 128):
+            for k in range(H // 128):
+                g = w13[e, 128 * m:128 * m + 128, 128 * k:128 * k + 128]
+                u = w13[e, I + 128 * m:I + 128 * m + 128, 128 * k:128 * k + 128]
+                tiles1.append(image(np.concatenate([g, u])))
+        for m in range(H // 256):
+            for k in range(I // 128):
+                tiles2.append(image(w2[e, 256 * m:256 * m + 256, 128 * k:128 * k + 128]))
+    return np.concatenate(tiles1).ravel(), np.concatenate(tiles2).ravel()
+
+
+def test_prelayout_matches_restatement(fmoe):
+    geo = W.TINY  # H = 256, I = 128: 2 GEMM1 tiles and 2 GEMM2 tiles per expert
+    gpu, cpu, _ = _inputs(geo, 4, seed=8)
+    w13p, w2p = fmoe.prelayout_weights(gpu["gemm1_weights"], gpu["gemm2_weights"])
+    torch.cuda.synchronize()
+    e1, e2 = _prelayout_numpy(cpu["gemm1_weights"].view(torch.uint8).numpy(),
+                              cpu["gemm2_weights"].view(torch.uint8).numpy(), geo.inter)
+    assert np.array_equal(w13p.view(torch.uint8).cpu().numpy().ravel(), e1)
+    assert np.array_equal(w2p.view(torch.uint8).cpu().numpy().ravel(), e2)
+
+
+@pytest.mark.parametrize("T,skew,tile", [(1, 0, 0), (64, 0, 0), (200, 0, 64), (200, 0, 32),
+                                         (1024, 0, 128), (4096, 8, 0)])
+def test_prelaid_weights_same_bits(fmoe, T, skew, tile):
+    """Both GEMM families fed from pre-laid-out weights (one bulk copy per weight tile) give
+    the output of the tensor-map path bit for bit: the shared-memory images are the same."""
+    geo = W.DSV3
+    gpu, _, _ = _inputs(geo, T, seed=6, skew_hot=skew)
+    w13p, w2p = fmoe.prelayout_weights(gpu["gemm1_weights"], gpu["gemm2_weights"])
+    args = W.operator_args(gpu)
+    ref = fmoe.kernel(*args, 0, 2.5, tile_n=tile)
+    args[4], args[6] = w13p, w2p
+    out = fmoe.kernel(*args, 0, 2.5, tile_n=tile, prelaid=True)
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    if T == 64:
+        idx, w = fmoe.route(gpu["routing_logits"], gpu["routing_bias"], 8, 4, 8, 2.5,
+                            num_local_experts=geo.num_local)
+        routed = fmoe.forward_routed(idx, w, gpu["hidden_states"], gpu["hidden_states_scale"],
+                                     w13p, gpu["gemm1_weights_scale"], w2p,
+                                     gpu["gemm2_weights_scale"], 0, geo.num_experts, n_group=8,
+                                     topk_group=4, prelaid=True)
+        torch.cuda.synchronize()
+        assert torch.equal(routed, ref)
