@@ -19,7 +19,10 @@ tokens; the step time is the max over ranks (CUDA events), `value` counts all ra
              copy bandwidth or the FP8 dense rate measured live by fmoe_probe_fp8_mma_rate;
              the bound is whichever roofline time is longer
   ep_parity  32 tokens per rank of the step's output against the single-GPU operator run
-             on each rank's expert slice (local_expert_offset) and summed in rank order
+             on each rank's experts (local_expert_offset) and summed in rank order
+  placement  (N>1) which experts each rank owns: balanced by default (greedy on the
+             128-row tile counts of a calibration batch of other tokens), or contiguous
+             256/N slices with --placement contiguous
   cpu_baseline  (N=1) the CPU oracle (PyTorch fp32 dequantise reference) on this host's
              cores, a bounded sample: 64 tokens of the same layer
   sweep      (N=1) BASELINE configs 1, 2 and 4 on one 32-expert slice (T = 1..8192 and the
@@ -70,6 +73,7 @@ GEMM2_BYTES_PER_ROW = 2 * 2048 + 16 * 4 + 7168 * 2         # hi/lo C + scales in
 L2_FLUSH_BYTES = 256 << 20
 LAYER_TOKENS = 4096
 PARITY_TOKENS = 32
+CAL_SEED = 7777  # seed offset of the expert-placement calibration batch (N > 1)
 CPU_SAMPLE_TOKENS = 64
 RSF = 2.5
 
@@ -170,7 +174,8 @@ def layer_weights(seed: int, first: int, count: int, device="cuda"):
     return W.make_expert_slice(W.DSV3, seed, first, count, device=device)
 
 
-def layer_config(T: int, world: int, exchange: str) -> dict:
+def layer_config(T: int, world: int, exchange: str, placement: str = "balanced",
+                 host_sync: bool = False) -> dict:
     per = 256 // world
     cfg = {"workload": "config3_dsv3_full_layer", "tokens_per_rank": T, "hidden": H,
            "intermediate": I, "experts": 256, "experts_per_rank": per, "top_k": 8,
@@ -180,8 +185,15 @@ def layer_config(T: int, world: int, exchange: str) -> dict:
     if world > 1:
         cfg["collectives"] = (
             "rows stored into the peers' buffers over NVLink (CUDA IPC), counts all-gather and "
-            "one-element all-reduce barriers (NCCL)" if exchange == "p2p" else
+            "one-element all-reduce barriers (NCCL); " + (
+                "counts read on the host each step" if host_sync else
+                "row offsets and received-row counts computed on the device (no host round "
+                "trip per step)") if exchange == "p2p" else
             "NCCL all-to-all-v dispatch + combine, counts all-to-all")
+        cfg["placement"] = (
+            "balanced: experts assigned to ranks by longest-processing-time greedy on their "
+            "128-row tile counts in a calibration batch (other tokens, same layer)"
+            if placement == "balanced" else "contiguous 256/N-expert slices")
     return cfg
 
 
@@ -367,11 +379,13 @@ def max_over_ranks(x: float) -> float:
 
 
 # ---------------------------------------------------------------------------- checks
-def ep_parity(out, acts, weights, world, rank, per):
+def ep_parity(out, acts, weights, world, rank, per, layer=None):
     """The step's output for this rank's first PARITY_TOKENS tokens against the
-    single-GPU operator: every rank runs `fmoe_b200.kernel` on all ranks' sampled tokens
-    with its own expert slice (local_expert_offset = rank * per), the partials are summed
-    in fp32 in rank order and rounded to bf16. Tolerance atol = rtol = 2e-2 (bf16 output)."""
+    single-GPU operator: every rank runs the operator on all ranks' sampled tokens with its
+    own experts (`fmoe_b200.kernel` with local_expert_offset = rank * per for contiguous
+    slices; under a placement, the routing kernel, the ids mapped to placement positions
+    and `fmoe_b200.forward_routed` on the rank's experts), the partials are summed in fp32
+    in rank order and rounded to bf16. Tolerance atol = rtol = 2e-2 (bf16 output)."""
     n = PARITY_TOKENS
     names = W.OPERATOR_ARGS[:4]
     mine = {"routing_logits": acts["routing_logits"][:n].contiguous(),
@@ -391,8 +405,14 @@ def ep_parity(out, acts, weights, world, rank, per):
                  "hidden_states_scale": sc.contiguous()}
     else:
         allin = mine
-    part = fmoe_b200.kernel(*[allin[k] for k in names], *[weights[k] for k in W.OPERATOR_ARGS[4:]],
-                            rank * per, RSF)
+    wts = [weights[k] for k in W.OPERATOR_ARGS[4:]]
+    if layer is not None and layer.placement is not None:
+        idx, w = fmoe_b200.route(allin["routing_logits"], allin["routing_bias"], 8, 4, 8, RSF)
+        part = fmoe_b200.forward_routed(layer.place_ids(idx).contiguous(), w,
+                                        allin["hidden_states"], allin["hidden_states_scale"],
+                                        *wts, rank * per, 256)
+    else:
+        part = fmoe_b200.kernel(*[allin[k] for k in names], *wts, rank * per, RSF)
     if world > 1:
         parts = torch.empty(world, world * n, H, dtype=torch.bfloat16, device="cuda")
         dist.all_gather_into_tensor(parts, part)
@@ -413,7 +433,7 @@ def ep_parity(out, acts, weights, world, rank, per):
     return {"tokens_checked": n * world, "max_abs": round(float(stats[0]), 6),
             "rel_rms": round(float(stats[1]), 6), "ok": bool(stats[2] <= 0.0),
             "tolerance": "atol 2e-2 + rtol 2e-2 on the bf16 output",
-            "reference": ("single-GPU operator on each rank's expert slice, summed in rank "
+            "reference": ("single-GPU operator on each rank's experts, summed in rank "
                           "order" if world > 1 else
                           "single-GPU operator on the sampled tokens alone")}
 
@@ -500,9 +520,20 @@ def run_ep(args, world, rank, local, peaks):
     hbm, fp8, hbm_src, fp8_src = peaks
     T = args.tokens or LAYER_TOKENS
     per = 256 // world
-    weights = layer_weights(args.seed, rank * per, per)
     acts = layer_activations(args.seed, rank, T)
-    layer = ep.ExpertParallelMoE(weights=weights, exchange=args.exchange)
+    placement = None
+    if args.placement == "balanced":
+        # expert loads of a calibration batch: other tokens (seed offset), the same layer
+        cal = W.make_activations(W.DSV3, T, args.seed + CAL_SEED + 1009 * rank, device="cuda")
+        placement = ep.calibrate_placement(
+            lambda lg, b: fmoe_b200.route(lg, b, 8, 4, 8, RSF), cal["routing_logits"],
+            acts["routing_bias"], 256)
+        del cal
+    mine = placement[rank * per:(rank + 1) * per] if placement else range(rank * per,
+                                                                          (rank + 1) * per)
+    weights = W.make_expert_set(W.DSV3, args.seed, mine, device="cuda")
+    layer = ep.ExpertParallelMoE(weights=weights, exchange=args.exchange, placement=placement,
+                                 max_tokens=None if args.ep_host_sync else T)
     a4 = [acts[k] for k in W.OPERATOR_ARGS[:4]]
     for _ in range(args.warmup):
         layer.forward(*a4)
@@ -541,10 +572,11 @@ def run_ep(args, world, rank, local, peaks):
     g1["gemm2"] = g2
     g1["traffic"] = None
     g1["rank"] = rank
-    parity = ep_parity(out, acts, weights, world, rank, per)
+    parity = ep_parity(out, acts, weights, world, rank, per, layer)
     e2e_ms, e2e_serial, h2d, d2h = time_e2e(acts, weights, args.steps, args.warmup,
                                             lambda *a, out=None: layer.forward(*a))
-    line = base_line(args, world, T, ms_per_step, layer_config(T, world, args.exchange))
+    line = base_line(args, world, T, ms_per_step,
+                     layer_config(T, world, args.exchange, args.placement, args.ep_host_sync))
     line.update({
         "breakdown_ms_max_over_ranks": {"route": round(float(br[0]), 3),
                                         "dispatch": round(float(br[1]), 3),
@@ -693,6 +725,8 @@ def run_reference(args, world, rank, local, flush):
     line["config"]["parallelism"] = (f"replicas x{world} (the reference has no expert "
                                      "parallelism: every rank holds all 256 experts)"
                                      if world > 1 else line["config"]["parallelism"])
+    for k in ("collectives", "placement"):  # no exchange between the reference's replicas
+        line["config"].pop(k, None)
     line.update({
         "dtype": "e4m3 x e4m3 -> fp32 (reference: fp32 SIMT / f16 and tf32-class mma.sync)",
         "runs_on": ("cuda (B200): the reference implements the path only in CUDA "
@@ -810,6 +844,11 @@ def main():
                          "(config 4: 8); 0 = grouped top-k over random logits")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--placement", choices=("balanced", "contiguous"), default="balanced",
+                    help="N>1: expert placement over the ranks")
+    ap.add_argument("--ep-host-sync", action="store_true",
+                    help="N>1: size each step's exchange on the host (one device-to-host read "
+                         "of the counts per step) instead of the sync-free device offsets")
     ap.add_argument("--exchange", choices=("p2p", "nccl"), default="p2p",
                     help="expert-parallel runs (N > 1): rows over peer memory or NCCL all-to-all")
     ap.add_argument("--sweep-tiles", default="0",

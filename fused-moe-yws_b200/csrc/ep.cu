@@ -6,7 +6,8 @@
 // all-to-all; these kernels build what it sends and consume what it receives, so no step of
 // the exchange runs as a chain of framework ops:
 //
-//   fmoe_ep_plan     per-destination send lists from the routing (stable in token order)
+//   fmoe_ep_plan     per-destination send lists from the routing (stable in token order);
+//                    fmoe_ep_plan_placed first maps expert ids to placement positions
 //   fmoe_ep_pack     one payload row per (token, destination): FP8 row | block scales |
 //                    expert ids | weights
 //   fmoe_ep_unpack   received rows -> the operator's inputs (row-major FP8, [H/128, R]
@@ -14,8 +15,9 @@
 //   fmoe_ep_combine  each token's returned partial outputs summed in rank order in fp32,
 //                    cast to bf16 (tokens with no route get zeros)
 //
-// Rank d owns experts [d * e_per_rank, (d + 1) * e_per_rank); a token goes to every rank
-// owning at least one of its selected experts, once.
+// Rank d owns experts [d * e_per_rank, (d + 1) * e_per_rank) (ids, or placement positions
+// after fmoe_ep_plan_placed); a token goes to every rank owning at least one of its selected
+// experts, once.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -49,15 +51,24 @@ __device__ __forceinline__ uint32_t dest_mask(const int* idx, int64_t t, int K, 
 // One CTA. Pass 1 counts each destination's tokens; pass 2 gives every (token, destination)
 // its row in the send buffer: the destinations' segments in rank order, tokens ascending
 // inside a segment (a block-wide exclusive scan per destination and chunk of tokens).
-__global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(const int* idx, int64_t T, int K,
+// With an expert placement (expert_pos != null), every selected expert id is first
+// replaced in place by its position expert_pos[e]; ranks own ranges of positions.
+__global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(int* idx, int64_t T, int K,
                                                                int e_per_rank, int world,
-                                                               int* pos, int* tokens,
-                                                               int* counts) {
+                                                               const int* expert_pos,
+                                                               int num_experts, int* pos,
+                                                               int* tokens, int* counts) {
   __shared__ int s_cnt[kMaxWorld];
   __shared__ int s_base[kMaxWorld];
   __shared__ int s_warp[kPlanThreads / 32][kMaxWorld];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid < kMaxWorld) s_cnt[tid] = 0;
+  if (expert_pos) {
+    for (int64_t i = tid; i < T * K; i += kPlanThreads) {
+      const int e = idx[i];
+      if (e >= 0 && e < num_experts) idx[i] = __ldg(expert_pos + e);
+    }
+  }
   __syncthreads();
   // pass 1: per-destination totals
   for (int d = 0; d < world; ++d) {
@@ -142,11 +153,13 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const uint8_t* hidden, con
   }
 }
 
-// One CTA per received row.
+// One CTA per received row. R is the row capacity (the scale array's leading dimension);
+// with rows_dev, rows at or past *rows_dev are not copied.
 __global__ void __launch_bounds__(256) ep_unpack_kernel(const uint8_t* recv, int64_t R, int H,
                                                         int K, uint8_t* hs, float* sc, int* idx,
-                                                        float* w) {
+                                                        float* w, const int* rows_dev) {
   const int64_t r = blockIdx.x;
+  if (rows_dev && r >= (int64_t)*rows_dev) return;
   const int kb = H / kBlock;
   const int64_t row_bytes = (int64_t)H + 4 * kb + 8 * K;
   const uint8_t* src = recv + r * row_bytes;
@@ -249,6 +262,7 @@ __global__ void __launch_bounds__(256) ep_return_p2p_kernel(
     const __nv_bfloat16* part, int64_t R, int H, int world, const int64_t* src_start,
     __nv_bfloat16* const* peer_back, const int64_t* shift, int64_t capacity, int* err) {
   const int64_t r = blockIdx.x;
+  if (r >= src_start[world]) return;  // past the received rows (grid sized by a capacity)
   int s = 0;
   while (s + 1 < world && r >= src_start[s + 1]) ++s;
   const int64_t q = r + shift[s];
@@ -260,6 +274,41 @@ __global__ void __launch_bounds__(256) ep_return_p2p_kernel(
   uint4* dst = reinterpret_cast<uint4*>(peer_back[s] + q * H);
   for (int v = threadIdx.x; v < H / 8; v += blockDim.x) dst[v] = __ldg(src + v);
   __threadfence_system();
+}
+
+// Row offsets of the P2P exchange from every rank's per-destination counts, on the device
+// (no host round trip): m[s][d] = rows rank s sends to rank d (an int64 [world][world + 1]
+// all-gather of each rank's counts; the last column is not used). Writes tables =
+// {shift_pack[world], starts[world + 1], shift_ret[world]} and rows = starts[world]:
+//   starts[s]     = sum_{q < s} m[q][me]       (first row of source s in my receive buffer)
+//   shift_pack[d] = sum_{q < me} m[q][d] - sum_{q < d} m[me][q]
+//   shift_ret[s]  = sum_{q < me} m[s][q] - starts[s]
+__global__ void ep_offsets_kernel(const int64_t* m, int world, int me, int64_t* tables,
+                                  int* rows) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const int W1 = world + 1;
+  int64_t* shift_pack = tables;
+  int64_t* starts = tables + world;
+  int64_t* shift_ret = tables + 2 * world + 1;
+  int64_t run = 0;
+  for (int s = 0; s < world; ++s) {
+    starts[s] = run;
+    run += m[(int64_t)s * W1 + me];
+  }
+  starts[world] = run;
+  *rows = (int)run;
+  int64_t seg = 0;  // sum_{q < d} m[me][q]
+  for (int d = 0; d < world; ++d) {
+    int64_t src = 0;
+    for (int q = 0; q < me; ++q) src += m[(int64_t)q * W1 + d];
+    shift_pack[d] = src - seg;
+    seg += m[(int64_t)me * W1 + d];
+  }
+  for (int s = 0; s < world; ++s) {
+    int64_t base = 0;
+    for (int q = 0; q < me; ++q) base += m[(int64_t)s * W1 + q];
+    shift_ret[s] = base - starts[s];
+  }
 }
 
 int ep_fail(int code, const std::string& msg) {
@@ -284,22 +333,43 @@ bool ep_geometry_ok(int64_t T, int H, int K, int world) {
 
 using namespace fmoe;
 
-extern "C" int fmoe_ep_plan(const int* topk_idx, int64_t num_tokens, int top_k, int world,
-                            int experts_per_rank, int* pos, int* tokens, int* counts,
-                            void* stream) {
+static int ep_plan_impl(int* topk_idx, int64_t num_tokens, int top_k, int world,
+                        int experts_per_rank, const int* expert_pos, int num_experts, int* pos,
+                        int* tokens, int* counts, void* stream, const char* name) {
   if (!ep_geometry_ok(num_tokens, kBlock, top_k, world) || experts_per_rank <= 0)
-    return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_plan: bad geometry");
-  if (!counts) return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_plan: NULL pointer");
+    return ep_fail(FMOE_ERR_VALUE, std::string(name) + ": bad geometry");
+  if (expert_pos && num_experts != world * experts_per_rank)
+    return ep_fail(FMOE_ERR_VALUE,
+                   std::string(name) + ": num_experts != world * experts_per_rank");
+  if (!counts) return ep_fail(FMOE_ERR_VALUE, std::string(name) + ": NULL pointer");
   if (num_tokens == 0) {  // empty tensors may have NULL data: only the counts are written
     const cudaError_t e =
         cudaMemsetAsync(counts, 0, sizeof(int) * world, static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return ep_fail(FMOE_ERR_RUNTIME, cudaGetErrorString(e));
     return FMOE_OK;
   }
-  if (!topk_idx || !pos || !tokens) return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_plan: NULL pointer");
+  if (!topk_idx || !pos || !tokens)
+    return ep_fail(FMOE_ERR_VALUE, std::string(name) + ": NULL pointer");
   ep_plan_kernel<<<1, kPlanThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      topk_idx, num_tokens, top_k, experts_per_rank, world, pos, tokens, counts);
-  return ep_check_launch("fmoe_ep_plan");
+      topk_idx, num_tokens, top_k, experts_per_rank, world, expert_pos, num_experts, pos,
+      tokens, counts);
+  return ep_check_launch(name);
+}
+
+extern "C" int fmoe_ep_plan(const int* topk_idx, int64_t num_tokens, int top_k, int world,
+                            int experts_per_rank, int* pos, int* tokens, int* counts,
+                            void* stream) {
+  // the kernel writes topk_idx only when given a placement
+  return ep_plan_impl(const_cast<int*>(topk_idx), num_tokens, top_k, world, experts_per_rank,
+                      nullptr, 0, pos, tokens, counts, stream, "fmoe_ep_plan");
+}
+
+extern "C" int fmoe_ep_plan_placed(int* topk_idx, int64_t num_tokens, int top_k, int world,
+                                   int experts_per_rank, const int* expert_pos, int num_experts,
+                                   int* pos, int* tokens, int* counts, void* stream) {
+  if (!expert_pos) return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_plan_placed: NULL pointer");
+  return ep_plan_impl(topk_idx, num_tokens, top_k, world, experts_per_rank, expert_pos,
+                      num_experts, pos, tokens, counts, stream, "fmoe_ep_plan_placed");
 }
 
 extern "C" int fmoe_ep_pack(const void* hidden_states, const float* hidden_states_scale,
@@ -331,8 +401,36 @@ extern "C" int fmoe_ep_unpack(const void* recv, int64_t rows, int hidden_size, i
     return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_unpack: recv and hidden_states must be 16-byte aligned");
   ep_unpack_kernel<<<(unsigned)rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint8_t*>(recv), rows, hidden_size, top_k,
-      static_cast<uint8_t*>(hidden_states), hidden_states_scale, topk_idx, topk_w);
+      static_cast<uint8_t*>(hidden_states), hidden_states_scale, topk_idx, topk_w, nullptr);
   return ep_check_launch("fmoe_ep_unpack");
+}
+
+extern "C" int fmoe_ep_unpack_count(const void* recv, int64_t capacity_rows,
+                                    const int* rows_dev, int hidden_size, int top_k,
+                                    void* hidden_states, float* hidden_states_scale,
+                                    int* topk_idx, float* topk_w, void* stream) {
+  if (!ep_geometry_ok(capacity_rows, hidden_size, top_k, 1))
+    return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_unpack_count: bad geometry");
+  if (capacity_rows == 0) return FMOE_OK;
+  if (!recv || !rows_dev || !hidden_states || !hidden_states_scale || !topk_idx || !topk_w)
+    return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_unpack_count: NULL pointer");
+  if (reinterpret_cast<uintptr_t>(recv) % 16 || reinterpret_cast<uintptr_t>(hidden_states) % 16)
+    return ep_fail(FMOE_ERR_VALUE,
+                   "fmoe_ep_unpack_count: recv and hidden_states must be 16-byte aligned");
+  ep_unpack_kernel<<<(unsigned)capacity_rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(recv), capacity_rows, hidden_size, top_k,
+      static_cast<uint8_t*>(hidden_states), hidden_states_scale, topk_idx, topk_w, rows_dev);
+  return ep_check_launch("fmoe_ep_unpack_count");
+}
+
+extern "C" int fmoe_ep_offsets(const int64_t* counts_all, int world, int rank, int64_t* tables,
+                               int* rows, void* stream) {
+  if (world <= 0 || world > kMaxWorld || rank < 0 || rank >= world)
+    return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_offsets: bad world / rank");
+  if (!counts_all || !tables || !rows) return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_offsets: NULL pointer");
+  ep_offsets_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(counts_all, world, rank,
+                                                                     tables, rows);
+  return ep_check_launch("fmoe_ep_offsets");
 }
 
 extern "C" int fmoe_ep_combine(const void* back, const int* pos, int64_t num_tokens,

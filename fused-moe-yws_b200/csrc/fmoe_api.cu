@@ -233,6 +233,7 @@ RouteArgs route_args(const fmoe_problem* p, const Carved& c, const float* logits
   RouteArgs a;
   a.in_idx = nullptr;
   a.in_w = nullptr;
+  a.t_dev = nullptr;
   a.inject_err = 0;
   a.logits = logits;
   a.bias = static_cast<const uint16_t*>(bias);
@@ -262,7 +263,8 @@ RouteArgs route_args(const fmoe_problem* p, const Carved& c, const float* logits
 
 int launch_route(const fmoe_problem* p, const Carved& c, const float* logits, const void* bias,
                  int bn, cudaStream_t stream, const int* in_idx = nullptr,
-                 const float* in_w = nullptr, int inject_err = 0) {
+                 const float* in_w = nullptr, int inject_err = 0,
+                 const int* t_dev = nullptr) {
   // meta words and the stream-K counters are contiguous: one small memset per call
   FMOE_CUDA_TRY(cudaMemsetAsync(c.at<int>(c.L.meta), 0, c.L.counters - c.L.meta +
                                 kTileCounters * sizeof(int), stream));
@@ -270,6 +272,7 @@ int launch_route(const fmoe_problem* p, const Carved& c, const float* logits, co
   ra.in_idx = in_idx;
   ra.in_w = in_w;
   ra.inject_err = inject_err;
+  ra.t_dev = t_dev;
   FMOE_CUDA_TRY(launch_pdl(route_plan_kernel, dim3((unsigned)c.L.n_route_ctas),
                            dim3(kRouteTokensPerCta * 32), 0, stream, ra));
   return FMOE_OK;
@@ -309,8 +312,8 @@ extern "C" int fmoe_workspace_size(const fmoe_problem* p, size_t* bytes) {
 namespace fmoe {
 namespace {
 int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_idx,
-                const float* in_w, void* workspace, size_t workspace_bytes, void* stream_ptr,
-                bool prelaid) {
+                const float* in_w, const int32_t* t_dev, void* workspace,
+                size_t workspace_bytes, void* stream_ptr, bool prelaid) {
   int v = validate(p);
   if (v != FMOE_OK) return v;
   if (prelaid && p->hidden_size % 256 != 0)
@@ -347,7 +350,8 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   const int inject = g_inject_err;
   g_inject_err = 0;
   if ((v = mark_stage(0, stream)) != FMOE_OK) return v;
-  v = launch_route(p, c, t->routing_logits, t->routing_bias, bn, stream, in_idx, in_w, inject);
+  v = launch_route(p, c, t->routing_logits, t->routing_bias, bn, stream, in_idx, in_w, inject,
+                   t_dev);
   if (v != FMOE_OK) return v;
   if ((v = mark_stage(1, stream)) != FMOE_OK) return v;
 
@@ -470,6 +474,7 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   ca.top_k = p->top_k;
   ca.err_word = g.err;
   ca.err_sink = sink;
+  ca.t_dev = t_dev;
   if (T >= kCombineWideTokens)
     FMOE_CUDA_TRY(launch_pdl(combine_kernel<2>,
                              dim3((unsigned)T, (unsigned)((H / 8 + 255) / 256)), dim3(128), 0,
@@ -500,6 +505,7 @@ struct GraphKey {
   fmoe_tensors t;
   const void* in_idx;
   const void* in_w;
+  const void* t_dev;
   void* ws;
   size_t ws_bytes;
   void* stream;
@@ -544,13 +550,13 @@ cudaStream_t capture_stream(int device) {
 
 int forward_cached(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_idx,
                    const float* in_w, void* workspace, size_t workspace_bytes,
-                   void* stream_ptr, bool prelaid = false) {
+                   void* stream_ptr, bool prelaid = false, const int32_t* t_dev = nullptr) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if (!graph_cache_enabled() || g_stage_on || g_inject_err != 0 || !p || !t ||
       p->num_tokens <= 0 ||
       cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone)
-    return run_forward(p, t, in_idx, in_w, workspace, workspace_bytes, stream_ptr, prelaid);
+    return run_forward(p, t, in_idx, in_w, t_dev, workspace, workspace_bytes, stream_ptr, prelaid);
   GraphKey key;
   std::memset(&key, 0, sizeof(key));  // padding bytes take part in the comparison
   key.p = *p;
@@ -558,6 +564,7 @@ int forward_cached(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* 
   key.t = *t;
   key.in_idx = in_idx;
   key.in_w = in_w;
+  key.t_dev = t_dev;
   key.ws = workspace;
   key.ws_bytes = workspace_bytes;
   key.stream = stream_ptr;
@@ -585,16 +592,16 @@ int forward_cached(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* 
     }
     g_graphs.push_back(GraphEntry{key, nullptr, ++g_graph_clock});
     lock.unlock();
-    return run_forward(p, t, in_idx, in_w, workspace, workspace_bytes, stream_ptr, prelaid);
+    return run_forward(p, t, in_idx, in_w, t_dev, workspace, workspace_bytes, stream_ptr, prelaid);
   }
   // second sighting: capture on the library stream, then launch on the caller's stream
   cudaStream_t cs = capture_stream(key.device);
   if (!cs) {
     lock.unlock();
-    return run_forward(p, t, in_idx, in_w, workspace, workspace_bytes, stream_ptr, prelaid);
+    return run_forward(p, t, in_idx, in_w, t_dev, workspace, workspace_bytes, stream_ptr, prelaid);
   }
   FMOE_CUDA_TRY(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
-  const int v = run_forward(p, t, in_idx, in_w, workspace, workspace_bytes, cs, prelaid);
+  const int v = run_forward(p, t, in_idx, in_w, t_dev, workspace, workspace_bytes, cs, prelaid);
   cudaGraph_t graph = nullptr;
   const cudaError_t ec = cudaStreamEndCapture(cs, &graph);
   if (v != FMOE_OK) {
@@ -631,6 +638,16 @@ extern "C" int fmoe_forward_routed(const fmoe_problem* p, const int32_t* topk_id
                                    size_t workspace_bytes, void* stream_ptr) {
   if (!topk_idx || !topk_w) return fail(FMOE_ERR_VALUE, "topk_idx / topk_w must not be NULL");
   return forward_cached(p, t, topk_idx, topk_w, workspace, workspace_bytes, stream_ptr);
+}
+
+extern "C" int fmoe_forward_routed_count(const fmoe_problem* p, const int32_t* topk_idx,
+                                         const float* topk_w, const int32_t* num_tokens_dev,
+                                         const fmoe_tensors* t, void* workspace,
+                                         size_t workspace_bytes, void* stream_ptr) {
+  if (!topk_idx || !topk_w || !num_tokens_dev)
+    return fail(FMOE_ERR_VALUE, "topk_idx / topk_w / num_tokens_dev must not be NULL");
+  return forward_cached(p, t, topk_idx, topk_w, workspace, workspace_bytes, stream_ptr, false,
+                        num_tokens_dev);
 }
 
 extern "C" int fmoe_forward_prelaid(const fmoe_problem* p, const fmoe_tensors* t,

@@ -17,6 +17,8 @@ struct RouteArgs {
   const uint16_t* bias;    // [E] bf16 bits
   const int* in_idx;       // routed mode: given [T, K] expert ids (logits unused); else null
   const float* in_w;       // routed mode: given [T, K] weights
+  const int* t_dev;        // routed mode, or null: tokens actually present (<= T), read on the
+                           // device; tokens [*t_dev, T) get no route
   int64_t T;
   int E, n_group, topk_group, top_k, E_local, local_offset;
   float rsf;
@@ -86,6 +88,7 @@ struct CombineArgs {
   int H, top_k;
   const int* err_word;          // the call's device error word (meta[kMetaError])
   unsigned* err_sink;           // host-mapped {bits, count} of the device, or null
+  const int* t_dev;             // or null: output rows [*t_dev, T) are not written
 };
 
 // Host-mapped error sink, one per device: the combine kernel (the last kernel of every

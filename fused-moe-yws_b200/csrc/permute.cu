@@ -242,6 +242,7 @@ __global__ void __launch_bounds__(128) combine_kernel(CombineArgs a) {
     const int e = *reinterpret_cast<const volatile int*>(a.err_word);
     if (e != 0) report_device_error(a.err_sink, e);
   }
+  if (a.t_dev && t >= (int64_t)*a.t_dev) return;  // past the tokens actually present
   if (threadIdx.x < a.top_k) s_rows[threadIdx.x] = a.token_row[t * a.top_k + threadIdx.x];
   __syncthreads();
   // this CTA covers 8-element vectors [blockIdx.y * 128 * kCombineVec, + 128 * kCombineVec)

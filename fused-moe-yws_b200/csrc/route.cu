@@ -213,11 +213,13 @@ __global__ void __launch_bounds__(kWarps * 32) route_plan_kernel(RouteArgs a) {
 
   const int64_t t = (int64_t)blockIdx.x * kWarps + warp;
   if (t < a.T && a.in_idx) {
-    // routed mode: (expert, weight) pairs computed elsewhere (expert-parallel dispatch)
+    // routed mode: (expert, weight) pairs computed elsewhere (expert-parallel dispatch);
+    // with a device-side token count, the slots past it are marked unselected
+    const int64_t tn = a.t_dev ? (int64_t)*a.t_dev : a.T;
     if (lane < K) {
-      const int e = a.in_idx[t * K + lane];
+      const int e = t < tn ? a.in_idx[t * K + lane] : -1;
       a.topk_idx[t * K + lane] = e;
-      a.topk_w[t * K + lane] = a.in_w[t * K + lane];
+      a.topk_w[t * K + lane] = t < tn ? a.in_w[t * K + lane] : 0.0f;
       const int le = e - a.local_offset;
       if (e >= 0 && le >= 0 && le < a.E_local) atomicAdd(&s_cnt[le], 1);
     }

@@ -140,6 +140,7 @@ extern "C" int fmoe_route_static(const fmoe_problem* p, const float* routing_log
   RouteArgs a;
   a.in_idx = nullptr;
   a.in_w = nullptr;
+  a.t_dev = nullptr;
   a.inject_err = 0;
   a.logits = routing_logits;
   a.bias = static_cast<const uint16_t*>(routing_bias);

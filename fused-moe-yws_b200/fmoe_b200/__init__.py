@@ -38,6 +38,8 @@ EXPORTED_SYMBOLS = ("fmoe_abi_version", "fmoe_last_error", "fmoe_validate", "fmo
                     "fmoe_ep_pack_p2p", "fmoe_ep_return_p2p", "fmoe_poll_device_error",
                     "fmoe_selftest_inject_device_error", "fmoe_probe_fp8_mma_rate",
                     "fmoe_tile_n", "fmoe_prelayout_weights", "fmoe_forward_prelaid",
+                    "fmoe_ep_plan_placed", "fmoe_forward_routed_count", "fmoe_ep_unpack_count",
+                    "fmoe_ep_offsets",
                     "fmoe_forward_routed_prelaid")
 
 
@@ -112,8 +114,14 @@ def load_library(path: Path | str | None = None):
         lib.fmoe_forward_routed_prelaid.argtypes = lib.fmoe_forward_routed.argtypes
         vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
         lib.fmoe_ep_plan.argtypes = [vp, i64, i32, i32, i32, vp, vp, vp, vp]
+        lib.fmoe_ep_plan_placed.argtypes = [vp, i64, i32, i32, i32, vp, i32, vp, vp, vp, vp]
         lib.fmoe_ep_pack.argtypes = [vp, vp, vp, vp, vp, i64, i32, i32, i32, vp, vp]
         lib.fmoe_ep_unpack.argtypes = [vp, i64, i32, i32, vp, vp, vp, vp, vp]
+        lib.fmoe_ep_unpack_count.argtypes = [vp, i64, vp, i32, i32, vp, vp, vp, vp, vp]
+        lib.fmoe_ep_offsets.argtypes = [vp, i32, i32, vp, vp, vp]
+        lib.fmoe_forward_routed_count.argtypes = [ctypes.POINTER(FmoeProblem), vp, vp, vp,
+                                                  ctypes.POINTER(FmoeTensors), vp,
+                                                  ctypes.c_size_t, vp]
         lib.fmoe_ep_combine.argtypes = [vp, vp, i64, i32, i32, vp, vp]
         lib.fmoe_ep_ipc_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp), vp]
         lib.fmoe_ep_ipc_open.argtypes = [vp, ctypes.POINTER(vp)]
@@ -339,10 +347,14 @@ def forward_routed(topk_idx, topk_w, hidden_states, hidden_states_scale, gemm1_w
                    gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
                    local_expert_offset: int, num_experts: int = 256, *, out=None,
                    tile_n: int = 0, n_group=None, topk_group=None,
-                   check: bool = False, prelaid: bool = False) -> torch.Tensor:
+                   check: bool = False, prelaid: bool = False,
+                   num_tokens_dev: torch.Tensor | None = None) -> torch.Tensor:
     """The operator on precomputed routing (``topk_idx`` int32 / ``topk_w`` fp32 [T, K]).
 
     Returns per-token sums over the local experts [offset, offset + E_local) in bf16.
+    With ``num_tokens_dev`` (int32 [1] on the device) T is a capacity and only the first
+    ``num_tokens_dev[0]`` tokens are processed (fmoe_forward_routed_count); the output rows
+    past them are left as they were.
     """
     T, K = topk_idx.shape
     EL, two_i, H = gemm1_weights.shape
@@ -372,9 +384,19 @@ def forward_routed(topk_idx, topk_w, hidden_states, hidden_states_scale, gemm1_w
                        gemm2_weights.data_ptr(), gemm2_weights_scale.data_ptr(), out.data_ptr())
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev).cuda_stream
-        fwd = lib.fmoe_forward_routed_prelaid if prelaid else lib.fmoe_forward_routed
-        rc = fwd(ctypes.byref(prob), topk_idx.data_ptr(), topk_w.data_ptr(), ctypes.byref(tens),
-                 ws.data_ptr(), ws.numel(), stream)
+        if num_tokens_dev is not None:
+            if prelaid:
+                raise ValueError("forward_routed: num_tokens_dev with prelaid weights is not "
+                                 "supported")
+            _check_tensor(num_tokens_dev, "num_tokens_dev", (1,), torch.int32)
+            rc = lib.fmoe_forward_routed_count(ctypes.byref(prob), topk_idx.data_ptr(),
+                                               topk_w.data_ptr(), num_tokens_dev.data_ptr(),
+                                               ctypes.byref(tens), ws.data_ptr(), ws.numel(),
+                                               stream)
+        else:
+            fwd = lib.fmoe_forward_routed_prelaid if prelaid else lib.fmoe_forward_routed
+            rc = fwd(ctypes.byref(prob), topk_idx.data_ptr(), topk_w.data_ptr(),
+                     ctypes.byref(tens), ws.data_ptr(), ws.numel(), stream)
     if rc != FMOE_OK:
         _raise(lib, rc, "forward_routed")
     if check:
@@ -443,16 +465,29 @@ def _stream(dev):
     return torch.cuda.current_stream(dev).cuda_stream
 
 
-def ep_plan(topk_idx: torch.Tensor, world: int, experts_per_rank: int):
-    """Send plan: (pos int32 [world, T], tokens int32 [sum], counts int32 [world])."""
+def ep_plan(topk_idx: torch.Tensor, world: int, experts_per_rank: int,
+            expert_pos: torch.Tensor | None = None):
+    """Send plan: (pos int32 [world, T], tokens int32 [sum], counts int32 [world]).
+
+    With ``expert_pos`` (int32 [world * experts_per_rank] on the device: each expert's
+    position in an expert placement) the ids in ``topk_idx`` are first replaced in place by
+    their positions (fmoe_ep_plan_placed)."""
     T, K = topk_idx.shape
     dev = topk_idx.device
     lib = load_library()
     pos = torch.empty(world, T, dtype=torch.int32, device=dev)
     tokens = torch.empty(max(T * world, 1), dtype=torch.int32, device=dev)
     counts = torch.empty(world, dtype=torch.int32, device=dev)
-    rc = lib.fmoe_ep_plan(topk_idx.data_ptr(), T, K, world, experts_per_rank, pos.data_ptr(),
-                          tokens.data_ptr(), counts.data_ptr(), _stream(dev))
+    if expert_pos is not None:
+        _check_tensor(expert_pos, "expert_pos", (world * experts_per_rank,), torch.int32)
+        if not topk_idx.is_contiguous():
+            raise ValueError("ep_plan: topk_idx must be contiguous (it is remapped in place)")
+        rc = lib.fmoe_ep_plan_placed(topk_idx.data_ptr(), T, K, world, experts_per_rank,
+                                     expert_pos.data_ptr(), expert_pos.numel(), pos.data_ptr(),
+                                     tokens.data_ptr(), counts.data_ptr(), _stream(dev))
+    else:
+        rc = lib.fmoe_ep_plan(topk_idx.data_ptr(), T, K, world, experts_per_rank,
+                              pos.data_ptr(), tokens.data_ptr(), counts.data_ptr(), _stream(dev))
     if rc != FMOE_OK:
         _raise(lib, rc, "ep_plan")
     return pos, tokens, counts
@@ -491,6 +526,48 @@ def ep_unpack(recv, H: int, K: int, rows: int = None, device=None):
     if rc != FMOE_OK:
         _raise(lib, rc, "ep_unpack")
     return hs, sc, idx, w
+
+
+def ep_unpack_count(recv, capacity_rows: int, rows_dev: torch.Tensor, H: int, K: int,
+                    out=None, device=None):
+    """fmoe_ep_unpack_count: the first rows_dev[0] received rows into arrays sized for
+    `capacity_rows` rows -- (hidden fp8 [cap, H], scale fp32 [H/128, cap], idx, w), or into
+    `out` (the same four tensors, reused across calls). `recv`: tensor or raw pointer."""
+    if isinstance(recv, int):
+        dev, ptr = device, recv
+    else:
+        dev, ptr = recv.device, recv.data_ptr()
+    lib = load_library()
+    if out is None:
+        out = (torch.empty(capacity_rows, H, dtype=torch.float8_e4m3fn, device=dev),
+               torch.empty(H // 128, capacity_rows, dtype=torch.float32, device=dev),
+               torch.empty(capacity_rows, K, dtype=torch.int32, device=dev),
+               torch.empty(capacity_rows, K, dtype=torch.float32, device=dev))
+    hs, sc, idx, w = out
+    _check_tensor(rows_dev, "rows_dev", (1,), torch.int32)
+    rc = lib.fmoe_ep_unpack_count(ptr, capacity_rows, rows_dev.data_ptr(), H, K, hs.data_ptr(),
+                                  sc.data_ptr(), idx.data_ptr(), w.data_ptr(), _stream(dev))
+    if rc != FMOE_OK:
+        _raise(lib, rc, "ep_unpack_count")
+    return out
+
+
+def ep_offsets(counts_all: torch.Tensor, rank: int, tables=None, rows=None):
+    """fmoe_ep_offsets: (tables int64 [3 world + 1], rows int32 [1]) on the device from the
+    int64 [world, world + 1] all-gather of the ranks' per-destination counts."""
+    world = counts_all.shape[0]
+    dev = counts_all.device
+    _check_tensor(counts_all, "counts_all", (world, world + 1), torch.int64)
+    if tables is None:
+        tables = torch.empty(3 * world + 1, dtype=torch.int64, device=dev)
+    if rows is None:
+        rows = torch.empty(1, dtype=torch.int32, device=dev)
+    lib = load_library()
+    rc = lib.fmoe_ep_offsets(counts_all.data_ptr(), world, rank, tables.data_ptr(),
+                             rows.data_ptr(), _stream(dev))
+    if rc != FMOE_OK:
+        _raise(lib, rc, "ep_offsets")
+    return tables, rows
 
 
 def ep_combine(back, pos: torch.Tensor, T: int, H: int = None):

@@ -19,6 +19,16 @@ GPU over `torch.distributed` (NCCL on B200s, gloo for the CPU tests):
 The token order inside every message is ascending token id, so dispatch, compute and
 combine are all deterministic.
 
+Expert placement: by default rank r owns the contiguous experts [r*E/N, (r+1)*E/N), the
+reference's slice (`local_expert_offset = r*E/N`). Routing skew makes those slices unequal
+(with the DS-V3 config-3 workload the busiest of 8 slices has 1.3x the mean rows), and every
+step waits for the busiest rank. `placement` assigns any E/N experts to each rank instead
+(rank r owns placement[r*E/N : (r+1)*E/N], its weights stacked in that order);
+`balanced_placement` computes one from per-expert row counts, such as those of a
+calibration batch (`calibrate_placement`). Internally each routed expert id is replaced by
+its position in the placement, so the destination rank is position // (E/N) and the local
+operator runs with local_expert_offset = r*E/N, exactly as for the contiguous slices.
+
 On CUDA the send plan, the payload packing and unpacking and the rank-ordered combine are
 kernels of the library (`fmoe_ep_*` in include/fmoe.h: one launch each, instead of chains
 of framework ops). With more than one rank the rows move over peer memory by default
@@ -71,19 +81,65 @@ def unpack_rows(buf, H, K):
     return hs, sc, ii, ww
 
 
+def placement_cost(rows: torch.Tensor, tile_rows: int = 128) -> torch.Tensor:
+    """Relative GEMM time of each expert: its routed rows in 128-row token tiles (every tile
+    streams the expert's full weights through the tensor cores once)."""
+    return (rows.to(torch.int64) + tile_rows - 1) // tile_rows
+
+
+def balanced_placement(rows, world: int) -> list:
+    """An expert placement for `world` ranks (E/world experts each) that evens out the
+    ranks' GEMM work: experts by decreasing `placement_cost`, each to the rank with the
+    least work so far that still has a free slot (longest-processing-time greedy; ties to
+    the lower expert id and the lower rank, so every rank computes the same placement).
+    Returns the E expert ids in rank-major order."""
+    rows = torch.as_tensor(rows).to(torch.int64).cpu()
+    E = rows.numel()
+    if E % world:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    per = E // world
+    cost = placement_cost(rows).tolist()
+    order = sorted(range(E), key=lambda e: (-cost[e], e))
+    work = [0] * world
+    owned = [[] for _ in range(world)]
+    for e in order:
+        r = min((r for r in range(world) if len(owned[r]) < per), key=lambda r: (work[r], r))
+        owned[r].append(e)
+        work[r] += cost[e]
+    return [e for r in range(world) for e in sorted(owned[r])]
+
+
+def calibrate_placement(route_fn: RouteFn, routing_logits, routing_bias, num_experts: int,
+                        group=None) -> list:
+    """Route a calibration batch on every rank, add the per-expert row counts over the
+    ranks and return `balanced_placement` of the totals (the same list on every rank)."""
+    idx, _ = route_fn(routing_logits, routing_bias)
+    idx = idx.reshape(-1).long()
+    rows = torch.bincount(idx[idx >= 0], minlength=num_experts).to(torch.int64)
+    if dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(rows, group=group)
+        world = dist.get_world_size(group)
+    else:
+        world = 1
+    return balanced_placement(rows, world)
+
+
 class ExpertParallelMoE:
     """The 256-expert layer sharded over the ranks of `group` by expert.
 
     `route_fn(logits, bias) -> (idx int32 [T, K], w fp32 [T, K])` and
     `local_fn(idx, w, hidden, scale, local_offset) -> bf16 [R, H]` default to the B200
     kernels of this package; tests pass CPU restatements to exercise the exchange logic.
+    `placement` (E expert ids, rank-major; None = contiguous slices) decides which experts
+    each rank owns; `weights` hold this rank's experts in `local_experts()` order, and
+    `local_fn` sees expert ids replaced by their placement positions.
     """
 
     def __init__(self, num_experts: int = 256, n_group: int = 8, topk_group: int = 4,
                  top_k: int = 8, routed_scaling_factor: float = 2.5, group=None,
                  weights: Optional[dict] = None, route_fn: Optional[RouteFn] = None,
                  local_fn: Optional[LocalFn] = None, fused_exchange: bool = True,
-                 exchange: str = "p2p"):
+                 exchange: str = "p2p", placement=None, max_tokens: Optional[int] = None):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -102,6 +158,22 @@ class ExpertParallelMoE:
         if exchange not in ("p2p", "nccl"):
             raise ValueError(f"exchange must be 'p2p' or 'nccl', not {exchange!r}")
         self.exchange = exchange
+        self.placement = None
+        self._pos = None           # expert id -> placement position (None: identity)
+        if placement is not None:
+            pl = [int(e) for e in placement]
+            if sorted(pl) != list(range(num_experts)):
+                raise ValueError("placement must list every expert exactly once")
+            if pl != list(range(num_experts)):
+                self.placement = pl
+                pos = [0] * num_experts
+                for i, e in enumerate(pl):
+                    pos[e] = i
+                self._pos = torch.tensor(pos, dtype=torch.int32)
+        if max_tokens is not None and max_tokens <= 0:
+            raise ValueError("max_tokens must be positive")
+        self.max_tokens = max_tokens
+        self._static = None      # device-side offset state of the host-sync-free P2P step
         self._peers = None       # fmoe_b200.PeerBuffers, sized for _cap_tokens per rank
         self._cap_tokens = 0
         self._flag = None
@@ -111,6 +183,27 @@ class ExpertParallelMoE:
         self.local_stage_ms = None
         self.last_local_tokens = self.last_local_rows = self.last_local_active = 0
 
+    def local_experts(self) -> list:
+        """Global ids of the experts this rank owns, in the order its weights are stacked."""
+        lo = self.local_offset
+        if self.placement is None:
+            return list(range(lo, lo + self.e_per_rank))
+        return self.placement[lo:lo + self.e_per_rank]
+
+    def place_ids(self, idx: torch.Tensor) -> torch.Tensor:
+        """Expert ids -> placement positions (unselected slots, < 0, stay as they are)."""
+        if self._pos is None:
+            return idx
+        if self._pos.device != idx.device:
+            self._pos = self._pos.to(idx.device)
+        return torch.where(idx >= 0, self._pos[idx.clamp_min(0).long()], idx)
+
+    def _dev_pos(self, dev):
+        """The placement positions on `dev` (None for contiguous slices)."""
+        if self._pos is not None and self._pos.device != dev:
+            self._pos = self._pos.to(dev)
+        return self._pos
+
     # ---- default B200 implementations --------------------------------------------------
     def _route_gpu(self, logits, bias):
         import fmoe_b200
@@ -119,14 +212,15 @@ class ExpertParallelMoE:
                                self.rsf, num_local_experts=self.e_per_rank,
                                local_expert_offset=self.local_offset)
 
-    def _local_gpu(self, idx, w, hs, sc, offset):
+    def _local_gpu(self, idx, w, hs, sc, offset, count=None, out=None):
         import fmoe_b200
 
         ws = self.weights
         return fmoe_b200.forward_routed(idx, w, hs, sc, ws["gemm1_weights"],
                                         ws["gemm1_weights_scale"], ws["gemm2_weights"],
                                         ws["gemm2_weights_scale"], offset, self.num_experts,
-                                        n_group=self.n_group, topk_group=self.topk_group)
+                                        n_group=self.n_group, topk_group=self.topk_group,
+                                        num_tokens_dev=count, out=out)
 
     # ---- peer-memory exchange -----------------------------------------------------------
     def _barrier(self):
@@ -163,6 +257,7 @@ class ExpertParallelMoE:
             torch.cuda.synchronize()
             self._peers.close()
             self._peers = None
+            self._static = None
 
     def _forward_p2p(self, idx, w, hidden_states, hidden_states_scale, mark):
         import fmoe_b200
@@ -170,7 +265,7 @@ class ExpertParallelMoE:
         T, H = hidden_states.shape
         K, world, me = self.top_k, self.world, self.rank
         dev = hidden_states.device
-        pos, _, counts = fmoe_b200.ep_plan(idx, world, self.e_per_rank)
+        pos, _, counts = fmoe_b200.ep_plan(idx, world, self.e_per_rank, self._dev_pos(dev))
         meta = torch.cat([counts.to(torch.int64),
                           torch.tensor([T], dtype=torch.int64, device=dev)])
         allm = torch.empty(world, world + 1, dtype=torch.int64, device=dev)
@@ -211,22 +306,80 @@ class ExpertParallelMoE:
         self._barrier()
         return fmoe_b200.ep_combine(self._peers.back[me], pos, T, H)
 
-    def _local(self, idx_r, w_r, hs_r, sc_r):
-        """The rank's own experts on what it received. In a timed pass on CUDA with the
-        default kernels, also records the operator's stage times (route, permute, gemm1,
-        gemm2, combine) and the received tokens, routed rows and active experts."""
-        if not (self._timed and hs_r.device.type == "cuda" and self.local_fn == self._local_gpu):
-            return self.local_fn(idx_r, w_r, hs_r, sc_r, self.local_offset)
+    def _forward_p2p_static(self, idx, w, hidden_states, hidden_states_scale, mark):
+        """The P2P step without a host round trip (`max_tokens` set): buffers sized once for
+        max_tokens per rank; the per-destination counts are all-gathered on the device, the
+        row offsets and the received row count computed there (fmoe_ep_offsets), and the
+        unpack and the local operator take that count from device memory, so the host only
+        enqueues work and the local operator replays one cached graph."""
         import fmoe_b200
 
+        T, H = hidden_states.shape
+        K, world, me = self.top_k, self.world, self.rank
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens exceed max_tokens={self.max_tokens}")
+        dev = hidden_states.device
+        if self._static is None:
+            self._ensure_peers(self.max_tokens, H, K, dev)  # collective, same size on every rank
+            cap = self._cap_tokens * world
+            self._static = {
+                "cap": cap,
+                "meta": torch.zeros(world + 1, dtype=torch.int64, device=dev),
+                "allm": torch.empty(world, world + 1, dtype=torch.int64, device=dev),
+                "tables": torch.empty(3 * world + 1, dtype=torch.int64, device=dev),
+                "rows": torch.zeros(1, dtype=torch.int32, device=dev),
+                "unpacked": (torch.empty(cap, H, dtype=torch.float8_e4m3fn, device=dev),
+                             torch.empty(H // 128, cap, dtype=torch.float32, device=dev),
+                             torch.empty(cap, K, dtype=torch.int32, device=dev),
+                             torch.empty(cap, K, dtype=torch.float32, device=dev)),
+                "part": torch.empty(cap, H, dtype=torch.bfloat16, device=dev),
+            }
+        st = self._static
+        cap = st["cap"]
+        pos, _, counts = fmoe_b200.ep_plan(idx, world, self.e_per_rank, self._dev_pos(dev))
+        st["meta"][:world].copy_(counts)
+        dist.all_gather_into_tensor(st["allm"], st["meta"], group=self.group)
+        tables, rows = fmoe_b200.ep_offsets(st["allm"], me, st["tables"], st["rows"])
+        self._err.zero_()
+        fmoe_b200.ep_pack_p2p(hidden_states, hidden_states_scale, idx, w, pos, self._peers,
+                              tables[:world], cap, self._err)
+        self._barrier()
+        hs_r, sc_r, idx_r, w_r = fmoe_b200.ep_unpack_count(self._peers.recv[me], cap, rows, H, K,
+                                                           out=st["unpacked"], device=dev)
+        mark()
+        part = self._local(idx_r, w_r, hs_r, sc_r, count=rows, out=st["part"])
+        mark()
+        fmoe_b200.ep_return_p2p(part, tables[world:2 * world + 1], self._peers,
+                                tables[2 * world + 1:], cap, self._err)
+        self._barrier()
+        return fmoe_b200.ep_combine(self._peers.back[me], pos, T, H)
+
+    def _local(self, idx_r, w_r, hs_r, sc_r, count=None, out=None):
+        """The rank's own experts on what it received (`count`: device token count, the
+        tensors then sized for a capacity). In a timed pass on CUDA with the default
+        kernels, also records the operator's stage times (route, permute, gemm1, gemm2,
+        combine) and the received tokens, routed rows and active experts."""
+        if count is not None:
+            if self.local_fn != self._local_gpu:
+                raise ValueError("a device-side token count needs the default local operator")
+            run = lambda: self._local_gpu(idx_r, w_r, hs_r, sc_r, self.local_offset,  # noqa
+                                          count=count, out=out)
+        else:
+            run = lambda: self.local_fn(idx_r, w_r, hs_r, sc_r, self.local_offset)  # noqa
+        if not (self._timed and hs_r.device.type == "cuda" and self.local_fn == self._local_gpu):
+            return run()
+        import fmoe_b200
+
+        n = int(count.item()) if count is not None else int(idx_r.shape[0])
         lo, hi = self.local_offset, self.local_offset + self.e_per_rank
-        sel = idx_r[(idx_r >= lo) & (idx_r < hi)]
-        self.last_local_tokens = int(idx_r.shape[0])
+        ids = idx_r[:n]
+        sel = ids[(ids >= lo) & (ids < hi)]
+        self.last_local_tokens = n
         self.last_local_rows = int(sel.numel())
         self.last_local_active = int(torch.unique(sel).numel())
         st = fmoe_b200.StageTimer()
         with st:
-            part = self.local_fn(idx_r, w_r, hs_r, sc_r, self.local_offset)
+            part = run()
         torch.cuda.synchronize()
         self.local_stage_ms = st.times_ms()
         return part
@@ -250,10 +403,13 @@ class ExpertParallelMoE:
         idx, w = self.route_fn(routing_logits, routing_bias)
         idx = idx.to(torch.int32).contiguous()
         w = w.to(torch.float32).contiguous()
-        mark()
         fused = self.fused_exchange and dev.type == "cuda"
+        if not fused:
+            idx = self.place_ids(idx)  # (fused: fmoe_ep_plan_placed maps the ids in place)
+        mark()
         if fused and self.world > 1 and self.exchange == "p2p":
-            res = self._forward_p2p(idx, w, hidden_states, hidden_states_scale, mark)
+            step = self._forward_p2p_static if self.max_tokens else self._forward_p2p
+            res = step(idx, w, hidden_states, hidden_states_scale, mark)
             mark()
             if timed and len(ev) == 5:
                 torch.cuda.synchronize()
@@ -263,7 +419,8 @@ class ExpertParallelMoE:
         if fused:
             import fmoe_b200
 
-            pos, _, counts = fmoe_b200.ep_plan(idx, self.world, self.e_per_rank)
+            pos, _, counts = fmoe_b200.ep_plan(idx, self.world, self.e_per_rank,
+                                               self._dev_pos(dev))
             send_counts = counts.to(torch.int64)
         else:
             # destinations: rank owning each selected expert (unselected slots are -1)

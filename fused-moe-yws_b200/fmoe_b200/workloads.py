@@ -126,13 +126,21 @@ def make_expert_slice(geo: Geometry, seed: int, first: int, count: int, device="
     """Weights of global experts [first, first + count) (expert-parallel rank slice); the
     values are those `make_weights` gives the same experts, since each expert has its own
     generator keyed by (seed, expert id)."""
-    H, I = geo.hidden, geo.inter
+    return make_expert_set(geo, seed, range(first, first + count), device)
+
+
+def make_expert_set(geo: Geometry, seed: int, experts, device="cpu"):
+    """Weights of the global experts `experts`, stacked in that order (an expert-parallel
+    rank's experts under any placement); each expert's values are those `make_weights`
+    gives it."""
+    experts = [int(e) for e in experts]
+    count, I, H = len(experts), geo.inter, geo.hidden
     w13 = torch.empty(count, 2 * I, H, dtype=torch.float8_e4m3fn, device=device)
     s13 = torch.empty(count, 2 * I // 128, H // 128, dtype=torch.float32, device=device)
     w2 = torch.empty(count, H, I, dtype=torch.float8_e4m3fn, device=device)
     s2 = torch.empty(count, H // 128, I // 128, dtype=torch.float32, device=device)
-    for j in range(count):
-        q13, a13, q2, a2 = make_expert(geo, seed, first + j, device)
+    for j, e in enumerate(experts):
+        q13, a13, q2, a2 = make_expert(geo, seed, e, device)
         w13[j].copy_(q13)
         s13[j].copy_(a13)
         w2[j].copy_(q2)

@@ -117,6 +117,16 @@ int fmoe_forward(const fmoe_problem* p, const fmoe_tensors* t, void* workspace,
 int fmoe_forward_routed(const fmoe_problem* p, const int32_t* topk_idx, const float* topk_w,
                         const fmoe_tensors* t, void* workspace, size_t workspace_bytes,
                         void* stream);
+/* fmoe_forward_routed with the token count on the device: p->num_tokens is a capacity (the
+ * sizes of every tensor and of the workspace), *num_tokens_dev (device int, 0 <=
+ * *num_tokens_dev <= p->num_tokens, written earlier on `stream`) the tokens present. Tokens
+ * past it get no route and their output rows are not written. Lets an expert-parallel step
+ * run without a host round trip for the received token count; repeated calls with the same
+ * buffers replay one cached graph. */
+int fmoe_forward_routed_count(const fmoe_problem* p, const int32_t* topk_idx,
+                              const float* topk_w, const int32_t* num_tokens_dev,
+                              const fmoe_tensors* t, void* workspace, size_t workspace_bytes,
+                              void* stream);
 
 /* Weight pre-layout (the weight side of the reference's per-call dequantise passes,
  * kernel.cu:924-1003, done once instead): writes every 32 KB weight tile the GEMMs load per
@@ -238,6 +248,15 @@ int fmoe_route_static(const fmoe_problem* p, const float* routing_logits,
  *   rank order, tokens ascending inside a group. */
 int fmoe_ep_plan(const int* topk_idx, int64_t num_tokens, int top_k, int world,
                  int experts_per_rank, int* pos, int* tokens, int* counts, void* stream);
+/* fmoe_ep_plan_placed: fmoe_ep_plan under an expert placement. expert_pos [num_experts]
+ * (num_experts = world * experts_per_rank) gives each expert's position in the placement
+ * (rank r owns positions [r * experts_per_rank, (r + 1) * experts_per_rank)); every
+ * selected id in topk_idx is replaced IN PLACE by its position first, so the payload rows
+ * and the receiving rank's fmoe_forward_routed (local_expert_offset = r * experts_per_rank,
+ * weights stacked in placement order) see positions. Ids < 0 are left as they are. */
+int fmoe_ep_plan_placed(int* topk_idx, int64_t num_tokens, int top_k, int world,
+                        int experts_per_rank, const int* expert_pos, int num_experts, int* pos,
+                        int* tokens, int* counts, void* stream);
 /* fmoe_ep_pack: one payload row per (token, rank) at the row pos[rank, token] of `send`.
  * hidden_states [T, H] FP8, hidden_states_scale [H/128, T]; both hidden_states and send
  * 16-byte aligned. */
@@ -250,6 +269,20 @@ int fmoe_ep_pack(const void* hidden_states, const float* hidden_states_scale,
 int fmoe_ep_unpack(const void* recv, int64_t rows, int hidden_size, int top_k,
                    void* hidden_states, float* hidden_states_scale, int* topk_idx,
                    float* topk_w, void* stream);
+/* fmoe_ep_unpack_count: the same for *rows_dev rows (a device int) into arrays sized for
+ * capacity_rows rows (hidden_states_scale [H/128, capacity_rows]); rows past the count are
+ * not written. */
+int fmoe_ep_unpack_count(const void* recv, int64_t capacity_rows, const int* rows_dev,
+                         int hidden_size, int top_k, void* hidden_states,
+                         float* hidden_states_scale, int* topk_idx, float* topk_w, void* stream);
+/* fmoe_ep_offsets: the P2P row offsets on the device from counts_all, the int64
+ * [world][world + 1] all-gather of every rank's per-destination counts (the last column is
+ * free for the caller): tables = {row_shift for fmoe_ep_pack_p2p [world], src_start for
+ * fmoe_ep_return_p2p [world + 1], row_shift for fmoe_ep_return_p2p [world]} (int64), and
+ * *rows = rows this rank receives (int32, for fmoe_ep_unpack_count and
+ * fmoe_forward_routed_count). */
+int fmoe_ep_offsets(const int64_t* counts_all, int world, int rank, int64_t* tables, int* rows,
+                    void* stream);
 /* fmoe_ep_combine: output [T, H] bf16 = per token, the bf16 partial rows back[pos[r, t]]
  * (rows in send order, as returned by the ranks) summed in fp32 in rank order starting from
  * 0, then rounded to bf16; tokens with no route get zeros. back and output 16-byte aligned. */
@@ -267,7 +300,8 @@ int fmoe_ep_combine(const void* back, const int* pos, int64_t num_tokens, int hi
  *   pos[d, t] + row_shift[d]; peer_recv and row_shift are device arrays of world entries.
  * fmoe_ep_return_p2p: received row r, from the source rank s with
  *   src_start[s] <= r < src_start[s + 1] (device array of world + 1), goes to peer_back[s] at
- *   row r + row_shift[s], as H bf16.
+ *   row r + row_shift[s], as H bf16. `rows` may be an upper bound: rows at or past
+ *   src_start[world] are skipped.
  * Rows outside [0, capacity_rows) are not written; they set bit 0 (pack) or 1 (return) of *err
  * (a device int the caller clears and reads). */
 int fmoe_ep_ipc_alloc(size_t bytes, void** ptr, void* handle);

@@ -48,7 +48,7 @@ def _geo():
                       n_group=NG, topk_group=KG, top_k=K)
 
 
-def _ep_worker(rank, world, port, T, result_q):
+def _ep_worker(rank, world, port, T, result_q, placement_mode=None):
     import oracle
     from fmoe_b200 import ep
     from fmoe_b200 import workloads as W
@@ -58,13 +58,24 @@ def _ep_worker(rank, world, port, T, result_q):
     geo = _geo()
     full = W.make_weights(geo, seed=9, device="cpu")
     per = GEO_E // world
-    sl = slice(rank * per, (rank + 1) * per)
-    local = {k: v[sl].contiguous() for k, v in full.items()}
     acts = W.make_activations(geo, T + rank, seed=100 + rank, device="cpu")
 
     def route_fn(logits, bias):
         idx, w = oracle.route(logits, bias, NG, KG, K, 2.5)
         return torch.from_numpy(idx), torch.from_numpy(w)
+
+    placement = None
+    if placement_mode == "shuffle":
+        placement = torch.randperm(GEO_E, generator=torch.Generator().manual_seed(5)).tolist()
+    elif placement_mode == "calibrated":
+        cal = W.make_activations(geo, 64, seed=700 + rank, device="cpu")
+        placement = ep.calibrate_placement(route_fn, cal["routing_logits"], acts["routing_bias"],
+                                           GEO_E)
+        allp = [None] * world
+        dist.all_gather_object(allp, placement)
+        assert all(p == placement for p in allp)
+    mine = placement[rank * per:(rank + 1) * per] if placement else list(range(rank * per, (rank + 1) * per))
+    local = {k: v[mine].contiguous() for k, v in full.items()}
 
     def local_fn(idx, w, hs, sc, offset):
         return oracle.moe_forward_routed(idx, w, hs, sc, local["gemm1_weights"],
@@ -73,7 +84,8 @@ def _ep_worker(rank, world, port, T, result_q):
 
     layer = ep.ExpertParallelMoE(num_experts=GEO_E, n_group=NG, topk_group=KG, top_k=K,
                                  routed_scaling_factor=2.5, route_fn=route_fn,
-                                 local_fn=local_fn)
+                                 local_fn=local_fn, placement=placement)
+    assert layer.local_experts() == mine
     out = layer.forward(acts["routing_logits"], acts["routing_bias"], acts["hidden_states"],
                         acts["hidden_states_scale"])
     ref = oracle.moe_forward(*W.operator_args({**acts, **full}), 0, 2.5, NG, KG, K)
@@ -85,12 +97,14 @@ def _ep_worker(rank, world, port, T, result_q):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_ep_matches_full_layer(world):
+@pytest.mark.parametrize("world,placement_mode", [(2, None), (4, None), (2, "shuffle"),
+                                                  (4, "calibrated")])
+def test_ep_matches_full_layer(world, placement_mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, 24, q)) for r in range(world)]
+    procs = [ctx.Process(target=_ep_worker, args=(r, world, port, 24, q, placement_mode))
+             for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=240) for _ in range(world)]
@@ -100,6 +114,41 @@ def test_ep_matches_full_layer(world):
     for rank, ok, rel, shape in sorted(results):
         assert shape == (24 + rank, GEO_H)
         assert ok and rel < 1e-2, (rank, rel)
+
+
+def test_balanced_placement():
+    from fmoe_b200 import ep
+
+    g = torch.Generator().manual_seed(3)
+    rows = (torch.rand(256, generator=g) ** 4 * 2000).to(torch.int64)  # skewed loads
+    rows[:10] = 0
+    for world in (1, 2, 4, 8):
+        pl = ep.balanced_placement(rows, world)
+        assert sorted(pl) == list(range(256))
+        per = 256 // world
+        cost = ep.placement_cost(rows)
+        work = [int(cost[pl[r * per:(r + 1) * per]].sum()) for r in range(world)]
+        contig = [int(cost[r * per:(r + 1) * per].sum()) for r in range(world)]
+        assert max(work) <= max(contig)
+        assert max(work) - min(work) <= int(cost.max())  # LPT bound on the spread
+        assert pl == ep.balanced_placement(rows.tolist(), world)  # deterministic
+    with pytest.raises(ValueError):
+        ep.balanced_placement(rows[:255], 2)
+
+
+def test_placement_validation():
+    from fmoe_b200 import ep
+
+    with pytest.raises(ValueError):
+        ep.ExpertParallelMoE(num_experts=16, n_group=4, topk_group=2, top_k=4,
+                             placement=list(range(15)) + [0])
+    layer = ep.ExpertParallelMoE(num_experts=16, n_group=4, topk_group=2, top_k=4,
+                                 placement=list(range(16)))
+    assert layer.placement is None and layer.local_experts() == list(range(16))
+    layer = ep.ExpertParallelMoE(num_experts=16, n_group=4, topk_group=2, top_k=4,
+                                 placement=list(reversed(range(16))))
+    idx = torch.tensor([[0, 15, -1, 3]], dtype=torch.int32)
+    assert layer.place_ids(idx).tolist() == [[15, 0, -1, 12]]
 
 
 def test_pack_unpack_roundtrip():

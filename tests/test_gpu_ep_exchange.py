@@ -57,6 +57,28 @@ def test_plan_matches_restatement(T, world):
         assert torch.equal(pos[d].long(), expect)
 
 
+@pytest.mark.parametrize("T,world", [(1, 2), (1500, 4), (4096, 8), (0, 2)])
+def test_placed_plan_equals_plan_of_mapped_ids(T, world):
+    """fmoe_ep_plan_placed: ids replaced in place by their placement positions (ids < 0
+    kept), then the same plan as fmoe_ep_plan of the mapped ids."""
+    import fmoe_b200
+    from fmoe_b200 import ep
+
+    E, K = 256, 8
+    idx, _ = _routing(T, K, E, world, seed=7 * T + world)
+    rows = torch.bincount(idx[idx >= 0].long().cpu(), minlength=E)
+    layer = ep.ExpertParallelMoE(num_experts=E, placement=ep.balanced_placement(rows, world)
+                                 if T else list(reversed(range(E))))
+    mapped = layer.place_ids(idx)
+    got = idx.clone()
+    pos, tokens, counts = fmoe_b200.ep_plan(got, world, E // world, layer._dev_pos(idx.device))
+    assert torch.equal(got, mapped)
+    pos_r, tokens_r, counts_r = fmoe_b200.ep_plan(mapped.clone(), world, E // world)
+    assert torch.equal(counts, counts_r)
+    n = int(counts_r.sum())
+    assert torch.equal(tokens[:n], tokens_r[:n]) and torch.equal(pos, pos_r)
+
+
 @pytest.mark.parametrize("H,K,T,world", [(7168, 8, 300, 4), (256, 4, 33, 2)])
 def test_pack_unpack_match_restatement(H, K, T, world):
     import fmoe_b200
@@ -111,6 +133,85 @@ def test_layer_same_with_and_without_exchange_kernels():
     plain = ep.ExpertParallelMoE(weights=weights, fused_exchange=False).forward(*a4)
     torch.cuda.synchronize()
     assert torch.equal(fused, plain)
+    # a placement (weights stacked in placement order) gives the same layer on one rank; the
+    # bits can differ only where the expert order moves a row into a stream-K split tile
+    pl = torch.randperm(256, generator=torch.Generator().manual_seed(4)).tolist()
+    wp = {k: v[pl].contiguous() for k, v in weights.items()}
+    placed = ep.ExpertParallelMoE(weights=wp, placement=pl).forward(*a4)
+    placed_plain = ep.ExpertParallelMoE(weights=wp, placement=pl,
+                                        fused_exchange=False).forward(*a4)
+    torch.cuda.synchronize()
+    assert torch.equal(placed, placed_plain)
+    torch.testing.assert_close(placed.float(), fused.float(), atol=1e-2, rtol=1e-2)
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+def test_offsets_match_host_arithmetic(world):
+    """fmoe_ep_offsets against the host-side offset arithmetic of the P2P step."""
+    import fmoe_b200
+
+    g = torch.Generator().manual_seed(world)
+    m = torch.randint(0, 500, (world, world + 1), generator=g, dtype=torch.int64)
+    cnt = m[:, :world].tolist()
+    for me in range(world):
+        tables, rows = fmoe_b200.ep_offsets(m.cuda(), me)
+
+        def src_start(d, s):
+            return sum(cnt[q][d] for q in range(s))
+
+        def seg_base(s, d):
+            return sum(cnt[s][:d])
+
+        starts = [src_start(me, s) for s in range(world + 1)]
+        expect = ([src_start(d, me) - seg_base(me, d) for d in range(world)] + starts +
+                  [seg_base(s, me) - starts[s] for s in range(world)])
+        assert tables.tolist() == expect and rows.item() == starts[world]
+
+
+def test_count_entry_points_match_exact_sizes():
+    """fmoe_ep_unpack_count and fmoe_forward_routed_count on capacity-sized buffers give the
+    first R rows exactly as fmoe_ep_unpack / fmoe_forward_routed on R rows."""
+    import fmoe_b200
+    from fmoe_b200 import workloads as W
+
+    H, K, R, cap, EL = 7168, 8, 300, 512, 32
+    row_bytes = fmoe_b200.ep_payload_bytes(H, K)
+    g = torch.Generator().manual_seed(11)
+    geo = W.DSV3
+    acts = W.make_activations(geo, R, 5, device="cuda")
+    idx, w = fmoe_b200.route(acts["routing_logits"], acts["routing_bias"], 8, 4, 8, 2.5)
+    recv = torch.randint(0, 255, (cap, row_bytes), generator=g, dtype=torch.uint8).cuda()
+    # real payload rows in front (valid FP8, scales, ids, weights)
+    pos, _, counts = fmoe_b200.ep_plan(idx, 1, 256)
+    recv[:R] = fmoe_b200.ep_pack(acts["hidden_states"], acts["hidden_states_scale"], idx, w,
+                                 pos, R)
+    rows = torch.tensor([R], dtype=torch.int32, device="cuda")
+    hs_c, sc_c, idx_c, w_c = fmoe_b200.ep_unpack_count(recv, cap, rows, H, K)
+    hs, sc, ii, ww = fmoe_b200.ep_unpack(recv[:R].contiguous(), H, K)
+    assert torch.equal(hs_c[:R].view(torch.uint8), hs.view(torch.uint8))
+    assert torch.equal(sc_c[:, :R], sc) and torch.equal(idx_c[:R], ii) and torch.equal(w_c[:R], ww)
+    wts = W.make_expert_slice(geo, 3, 0, EL, device="cuda")
+    wl = [wts[k] for k in W.OPERATOR_ARGS[4:]]
+    # stale ids past R must not be routed: fill them with a local expert
+    idx_c[R:] = 3
+    exact = fmoe_b200.forward_routed(ii, ww, hs, sc, *wl, 0, 256)
+    out = torch.full((cap, H), 7.0, dtype=torch.bfloat16, device="cuda")
+    for _ in range(3):  # eager, then captured, then replayed from the library's graph cache
+        got = fmoe_b200.forward_routed(idx_c, w_c, hs_c, sc_c, *wl, 0, 256, out=out,
+                                       num_tokens_dev=rows)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(got[:R].float(), exact.float(), atol=1e-2, rtol=1e-2)
+        assert bool((got[R:] == 7.0).all())  # rows past the count untouched
+    # the count is read at run time: a smaller count on the same buffers
+    rows.fill_(100)
+    got = fmoe_b200.forward_routed(idx_c, w_c, hs_c, sc_c, *wl, 0, 256, out=out,
+                                   num_tokens_dev=rows)
+    exact100 = fmoe_b200.forward_routed(ii[:100].contiguous(), ww[:100].contiguous(),
+                                        hs[:100].contiguous(), sc[:, :100].contiguous(), *wl, 0,
+                                        256)
+    torch.cuda.synchronize()
+    torch.testing.assert_close(got[:100].float(), exact100.float(), atol=1e-2, rtol=1e-2)
+    assert fmoe_b200.poll_device_error() == 0
 
 
 def test_exchange_entry_points_reject_bad_arguments():
@@ -118,6 +219,12 @@ def test_exchange_entry_points_reject_bad_arguments():
 
     lib = fmoe_b200.load_library()
     assert lib.fmoe_ep_plan(None, 4, 8, 2, 128, None, None, None, None) == fmoe_b200.FMOE_ERR_VALUE
+    assert lib.fmoe_ep_plan_placed(None, 4, 8, 2, 128, None, 256, None, None, None,
+                                   None) == fmoe_b200.FMOE_ERR_VALUE
+    assert lib.fmoe_ep_offsets(None, 2, 0, None, None, None) == fmoe_b200.FMOE_ERR_VALUE
+    assert lib.fmoe_ep_offsets(None, 2, 2, None, None, None) == fmoe_b200.FMOE_ERR_VALUE
+    assert lib.fmoe_ep_unpack_count(None, 3, None, 7168, 8, None, None, None, None,
+                                    None) == fmoe_b200.FMOE_ERR_VALUE
     assert lib.fmoe_ep_combine(None, None, 4, 7168, 0, None, None) == fmoe_b200.FMOE_ERR_VALUE
     assert lib.fmoe_ep_unpack(None, 3, 100, 8, None, None, None, None, None) == \
         fmoe_b200.FMOE_ERR_VALUE
