@@ -27,6 +27,13 @@ struct StreamK {
 // split by stream-K in K-step units so every CTA ends at the same time. Every role of a
 // CTA walks the same sequence. (Measured on B200: putting the split tiles first, or
 // starting whole tiles at a CTA-dependent K step, is slower at every T.)
+// A launch of G/2 .. G tiles runs them whole, one per CTA: the fix-up round trips of split
+// tiles (partial stores, fences, counters: microseconds each while the other CTAs saturate
+// HBM) cost more than the idle CTAs. Below G/2 tiles, splitting still wins: one CTA's
+// per-K-step issue and promotion cost caps it far below its share of HBM bandwidth, so
+// more CTAs must stream. (Decode calls on B200, graph-replayed device time: T = 1 66.8 ->
+// 61.4 us, T = 4 81.5 -> 73.7, T = 8 82 -> 74.5; whole tiles for every launch of <= G tiles
+// made T = 1 slower, its GEMM1 having 48 tiles.)
 struct Schedule {
   int KS, G, cta;
   int dp_tiles;  // whole-tile prefix, a multiple of G
@@ -38,7 +45,9 @@ struct Schedule {
     KS = ks;
     G = grid;
     cta = c;
-    dp_tiles = num_tiles > 2 * G ? (num_tiles / G - 1) * G : 0;
+    dp_tiles = num_tiles <= G && 2 * num_tiles >= G ? num_tiles
+               : num_tiles > 2 * G                      ? (num_tiles / G - 1) * G
+                                                        : 0;
     sk.W = (int64_t)(num_tiles - dp_tiles) * KS;
     sk.G = G;
     g = sk.start(c);

@@ -30,7 +30,10 @@ class Schedule:
 
     def __init__(self, num_tiles, ks, grid, c):
         self.KS, self.G, self.cta, self.num_tiles = ks, grid, c, num_tiles
-        self.dp_tiles = (num_tiles // grid - 1) * grid if num_tiles > 2 * grid else 0
+        if num_tiles <= grid and 2 * num_tiles >= grid:
+            self.dp_tiles = num_tiles  # G/2 .. G tiles: whole, one per CTA
+        else:
+            self.dp_tiles = (num_tiles // grid - 1) * grid if num_tiles > 2 * grid else 0
         self.sk = StreamK((num_tiles - self.dp_tiles) * ks, grid)
         self.g, self.g_end = self.sk.start(c), self.sk.start(c + 1)
         self.dp_next = c
@@ -135,6 +138,17 @@ def test_cta_of_inverts_start():
 def test_whole_tiles_are_a_multiple_of_the_grid():
     for n, G in itertools.product([1, 148, 296, 297, 444, 1000, 4096], [1, 148]):
         s = Schedule(n, 56, G, 0)
+        if G // 2 <= n <= G and 2 * n >= G:
+            assert s.dp_tiles == n  # one whole tile per CTA, nothing split
+            continue
         assert s.dp_tiles % G == 0 and 0 <= n - s.dp_tiles
         if n > 2 * G:
             assert G <= n - s.dp_tiles < 2 * G
+
+
+def test_few_tiles_run_whole_or_split_by_count():
+    G = 148
+    for n in range(1, 2 * G + 1):
+        s = Schedule(n, 56, G, 0)
+        whole = n <= G and 2 * n >= G
+        assert (s.dp_tiles == n) == whole and (s.dp_tiles == 0) == (not whole)
