@@ -427,7 +427,8 @@ extern "C" int fmoe_ep_offsets(const int64_t* counts_all, int world, int rank, i
                                int* rows, void* stream) {
   if (world <= 0 || world > kMaxWorld || rank < 0 || rank >= world)
     return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_offsets: bad world / rank");
-  if (!counts_all || !tables || !rows) return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_offsets: NULL pointer");
+  if (!counts_all || !tables || !rows)
+    return ep_fail(FMOE_ERR_VALUE, "fmoe_ep_offsets: NULL pointer");
   ep_offsets_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(counts_all, world, rank,
                                                                      tables, rows);
   return ep_check_launch("fmoe_ep_offsets");

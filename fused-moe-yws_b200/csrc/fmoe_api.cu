@@ -311,9 +311,20 @@ extern "C" int fmoe_workspace_size(const fmoe_problem* p, size_t* bytes) {
 
 namespace fmoe {
 namespace {
+// Expert-parallel return of the combine's rows to their source ranks (peer memory), or none.
+struct EpReturn {
+  void* const* peer_out;
+  const int64_t* src_start;
+  const int64_t* row_shift;
+  int world;
+  int64_t capacity;
+  int* err;
+};
+
 int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_idx,
                 const float* in_w, const int32_t* t_dev, void* workspace,
-                size_t workspace_bytes, void* stream_ptr, bool prelaid) {
+                size_t workspace_bytes, void* stream_ptr, bool prelaid,
+                const EpReturn* ret = nullptr) {
   int v = validate(p);
   if (v != FMOE_OK) return v;
   if (prelaid && p->hidden_size % 256 != 0)
@@ -375,11 +386,13 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   sa.a_perm = c.at<uint8_t>(c.L.a_perm);
   sa.a_scale = c.at<float>(c.L.a_scale);
   sa.meta = c.at<int>(c.L.meta);
+  int permute_ctas = 0;
   {
     // split each row's columns over enough CTAs to cover the SMs at small T
     const int sms = num_sms_current();
     int parts = (int)((2 * sms + c.L.n_route_ctas - 1) / c.L.n_route_ctas);
     parts = parts < 1 ? 1 : (parts > 28 ? 28 : parts);
+    permute_ctas = (int)c.L.n_route_ctas * parts;
     FMOE_CUDA_TRY(launch_pdl(scatter_gather_kernel,
                              dim3((unsigned)c.L.n_route_ctas, (unsigned)parts), dim3(256), 0,
                              stream, sa));
@@ -445,7 +458,13 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   g.w_scale = t->gemm1_weights_scale;
   g.act_scale = sa.a_scale;
   int64_t bound = c.L.max_chunks * (int64_t)g.m_tiles;
-  const int grid1 = (int)(bound < sms ? bound : sms);
+  // Decode family with a small permute grid (T <= 16: 28 CTAs): GEMM1 leaves the permute's
+  // SMs free. Its CTAs then all start while the permute runs and issue their first weight
+  // stages, instead of a quarter of them starting only when the permute has finished and
+  // ending last (T = 1: GEMM1's span after its wait 29 -> 26.7 us on B200).
+  int sms1 = sms;
+  if (!tm && permute_ctas * 4 <= sms) sms1 = sms - permute_ctas;
+  const int grid1 = (int)(bound < sms1 ? bound : sms1);
   if (tm)
     FMOE_CUDA_TRY(launch_gemm1_tm(m_a, m_w13, g, grid1, stream));
   else
@@ -475,6 +494,12 @@ int run_forward(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_
   ca.err_word = g.err;
   ca.err_sink = sink;
   ca.t_dev = t_dev;
+  ca.peer_out = ret ? reinterpret_cast<__nv_bfloat16* const*>(ret->peer_out) : nullptr;
+  ca.src_start = ret ? ret->src_start : nullptr;
+  ca.row_shift = ret ? ret->row_shift : nullptr;
+  ca.world = ret ? ret->world : 0;
+  ca.capacity = ret ? ret->capacity : 0;
+  ca.xerr = ret ? ret->err : nullptr;
   if (T >= kCombineWideTokens)
     FMOE_CUDA_TRY(launch_pdl(combine_kernel<2>,
                              dim3((unsigned)T, (unsigned)((H / 8 + 255) / 256)), dim3(128), 0,
@@ -506,6 +531,7 @@ struct GraphKey {
   const void* in_idx;
   const void* in_w;
   const void* t_dev;
+  EpReturn ret;
   void* ws;
   size_t ws_bytes;
   void* stream;
@@ -550,13 +576,15 @@ cudaStream_t capture_stream(int device) {
 
 int forward_cached(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* in_idx,
                    const float* in_w, void* workspace, size_t workspace_bytes,
-                   void* stream_ptr, bool prelaid = false, const int32_t* t_dev = nullptr) {
+                   void* stream_ptr, bool prelaid = false, const int32_t* t_dev = nullptr,
+                   const EpReturn* ret = nullptr) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
   if (!graph_cache_enabled() || g_stage_on || g_inject_err != 0 || !p || !t ||
       p->num_tokens <= 0 ||
       cudaStreamIsCapturing(stream, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone)
-    return run_forward(p, t, in_idx, in_w, t_dev, workspace, workspace_bytes, stream_ptr, prelaid);
+    return run_forward(p, t, in_idx, in_w, t_dev, workspace, workspace_bytes, stream_ptr,
+                       prelaid, ret);
   GraphKey key;
   std::memset(&key, 0, sizeof(key));  // padding bytes take part in the comparison
   key.p = *p;
@@ -565,6 +593,7 @@ int forward_cached(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* 
   key.in_idx = in_idx;
   key.in_w = in_w;
   key.t_dev = t_dev;
+  if (ret) std::memcpy(&key.ret, ret, sizeof(EpReturn));  // callers zero its padding
   key.ws = workspace;
   key.ws_bytes = workspace_bytes;
   key.stream = stream_ptr;
@@ -592,16 +621,19 @@ int forward_cached(const fmoe_problem* p, const fmoe_tensors* t, const int32_t* 
     }
     g_graphs.push_back(GraphEntry{key, nullptr, ++g_graph_clock});
     lock.unlock();
-    return run_forward(p, t, in_idx, in_w, t_dev, workspace, workspace_bytes, stream_ptr, prelaid);
+    return run_forward(p, t, in_idx, in_w, t_dev, workspace, workspace_bytes, stream_ptr,
+                       prelaid, ret);
   }
   // second sighting: capture on the library stream, then launch on the caller's stream
   cudaStream_t cs = capture_stream(key.device);
   if (!cs) {
     lock.unlock();
-    return run_forward(p, t, in_idx, in_w, t_dev, workspace, workspace_bytes, stream_ptr, prelaid);
+    return run_forward(p, t, in_idx, in_w, t_dev, workspace, workspace_bytes, stream_ptr,
+                       prelaid, ret);
   }
   FMOE_CUDA_TRY(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
-  const int v = run_forward(p, t, in_idx, in_w, t_dev, workspace, workspace_bytes, cs, prelaid);
+  const int v =
+      run_forward(p, t, in_idx, in_w, t_dev, workspace, workspace_bytes, cs, prelaid, ret);
   cudaGraph_t graph = nullptr;
   const cudaError_t ec = cudaStreamEndCapture(cs, &graph);
   if (v != FMOE_OK) {
@@ -648,6 +680,28 @@ extern "C" int fmoe_forward_routed_count(const fmoe_problem* p, const int32_t* t
     return fail(FMOE_ERR_VALUE, "topk_idx / topk_w / num_tokens_dev must not be NULL");
   return forward_cached(p, t, topk_idx, topk_w, workspace, workspace_bytes, stream_ptr, false,
                         num_tokens_dev);
+}
+
+extern "C" int fmoe_forward_routed_count_p2p(
+    const fmoe_problem* p, const int32_t* topk_idx, const float* topk_w,
+    const int32_t* num_tokens_dev, const fmoe_tensors* t, void* workspace,
+    size_t workspace_bytes, void* const* peer_out, const int64_t* src_start,
+    const int64_t* row_shift, int world, int64_t capacity_rows, int* err, void* stream_ptr) {
+  if (!topk_idx || !topk_w || !num_tokens_dev)
+    return fail(FMOE_ERR_VALUE, "topk_idx / topk_w / num_tokens_dev must not be NULL");
+  if (!peer_out || !src_start || !row_shift || !err || world <= 0 || world > 32 ||
+      capacity_rows < 0)
+    return fail(FMOE_ERR_VALUE, "fmoe_forward_routed_count_p2p: bad return arguments");
+  EpReturn ret;
+  std::memset(&ret, 0, sizeof(ret));  // the graph-cache key compares its bytes
+  ret.peer_out = peer_out;
+  ret.src_start = src_start;
+  ret.row_shift = row_shift;
+  ret.world = world;
+  ret.capacity = capacity_rows;
+  ret.err = err;
+  return forward_cached(p, t, topk_idx, topk_w, workspace, workspace_bytes, stream_ptr, false,
+                        num_tokens_dev, &ret);
 }
 
 extern "C" int fmoe_forward_prelaid(const fmoe_problem* p, const fmoe_tensors* t,

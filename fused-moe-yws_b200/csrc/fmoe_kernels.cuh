@@ -89,6 +89,15 @@ struct CombineArgs {
   const int* err_word;          // the call's device error word (meta[kMetaError])
   unsigned* err_sink;           // host-mapped {bits, count} of the device, or null
   const int* t_dev;             // or null: output rows [*t_dev, T) are not written
+  // Expert-parallel return, or null: row t goes to rank s's buffer peer_out[s] at row
+  // t + row_shift[s], s the source with src_start[s] <= t < src_start[s + 1] (rows outside
+  // [0, capacity) are dropped and set bit 1 of *xerr), instead of to out.
+  __nv_bfloat16* const* peer_out;
+  const int64_t* src_start;     // [world + 1]
+  const int64_t* row_shift;     // [world]
+  int world;
+  int64_t capacity;
+  int* xerr;
 };
 
 // Host-mapped error sink, one per device: the combine kernel (the last kernel of every

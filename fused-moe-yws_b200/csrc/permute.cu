@@ -243,6 +243,19 @@ __global__ void __launch_bounds__(128) combine_kernel(CombineArgs a) {
     if (e != 0) report_device_error(a.err_sink, e);
   }
   if (a.t_dev && t >= (int64_t)*a.t_dev) return;  // past the tokens actually present
+  __nv_bfloat16* dst = a.out + t * a.H;
+  if (a.peer_out) {
+    // expert-parallel return: straight into the source rank's buffer (peer memory)
+    if (t >= a.src_start[a.world]) return;
+    int s = 0;
+    while (s + 1 < a.world && t >= a.src_start[s + 1]) ++s;
+    const int64_t q = t + a.row_shift[s];
+    if (q < 0 || q >= a.capacity) {
+      if (threadIdx.x == 0 && blockIdx.y == 0) atomicOr(a.xerr, 2);
+      return;
+    }
+    dst = a.peer_out[s] + q * a.H;
+  }
   if (threadIdx.x < a.top_k) s_rows[threadIdx.x] = a.token_row[t * a.top_k + threadIdx.x];
   __syncthreads();
   // this CTA covers 8-element vectors [blockIdx.y * 128 * kCombineVec, + 128 * kCombineVec)
@@ -283,8 +296,9 @@ __global__ void __launch_bounds__(128) combine_kernel(CombineArgs a) {
     __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
 #pragma unroll
     for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[u][2 * j], acc[u][2 * j + 1]);
-    *reinterpret_cast<uint4*>(a.out + t * a.H + v * 8) = o;
+    *reinterpret_cast<uint4*>(dst + v * 8) = o;
   }
+  if (a.peer_out) __threadfence_system();  // the rows are read by the peer after a barrier
 }
 
 template __global__ void combine_kernel<1>(CombineArgs a);

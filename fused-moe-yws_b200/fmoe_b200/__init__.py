@@ -39,7 +39,7 @@ EXPORTED_SYMBOLS = ("fmoe_abi_version", "fmoe_last_error", "fmoe_validate", "fmo
                     "fmoe_selftest_inject_device_error", "fmoe_probe_fp8_mma_rate",
                     "fmoe_tile_n", "fmoe_prelayout_weights", "fmoe_forward_prelaid",
                     "fmoe_ep_plan_placed", "fmoe_forward_routed_count", "fmoe_ep_unpack_count",
-                    "fmoe_ep_offsets",
+                    "fmoe_ep_offsets", "fmoe_forward_routed_count_p2p",
                     "fmoe_forward_routed_prelaid")
 
 
@@ -122,6 +122,9 @@ def load_library(path: Path | str | None = None):
         lib.fmoe_forward_routed_count.argtypes = [ctypes.POINTER(FmoeProblem), vp, vp, vp,
                                                   ctypes.POINTER(FmoeTensors), vp,
                                                   ctypes.c_size_t, vp]
+        lib.fmoe_forward_routed_count_p2p.argtypes = [
+            ctypes.POINTER(FmoeProblem), vp, vp, vp, ctypes.POINTER(FmoeTensors), vp,
+            ctypes.c_size_t, vp, vp, vp, i32, i64, vp, vp]
         lib.fmoe_ep_combine.argtypes = [vp, vp, i64, i32, i32, vp, vp]
         lib.fmoe_ep_ipc_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp), vp]
         lib.fmoe_ep_ipc_open.argtypes = [vp, ctypes.POINTER(vp)]
@@ -348,13 +351,15 @@ def forward_routed(topk_idx, topk_w, hidden_states, hidden_states_scale, gemm1_w
                    local_expert_offset: int, num_experts: int = 256, *, out=None,
                    tile_n: int = 0, n_group=None, topk_group=None,
                    check: bool = False, prelaid: bool = False,
-                   num_tokens_dev: torch.Tensor | None = None) -> torch.Tensor:
+                   num_tokens_dev: torch.Tensor | None = None, return_to=None) -> torch.Tensor:
     """The operator on precomputed routing (``topk_idx`` int32 / ``topk_w`` fp32 [T, K]).
 
     Returns per-token sums over the local experts [offset, offset + E_local) in bf16.
     With ``num_tokens_dev`` (int32 [1] on the device) T is a capacity and only the first
     ``num_tokens_dev[0]`` tokens are processed (fmoe_forward_routed_count); the output rows
-    past them are left as they were.
+    past them are left as they were. ``return_to=(peers, src_start, row_shift, capacity_rows,
+    err)`` (with ``num_tokens_dev``) writes each output row straight into its source rank's
+    return buffer instead of ``out`` (fmoe_forward_routed_count_p2p).
     """
     T, K = topk_idx.shape
     EL, two_i, H = gemm1_weights.shape
@@ -389,10 +394,18 @@ def forward_routed(topk_idx, topk_w, hidden_states, hidden_states_scale, gemm1_w
                 raise ValueError("forward_routed: num_tokens_dev with prelaid weights is not "
                                  "supported")
             _check_tensor(num_tokens_dev, "num_tokens_dev", (1,), torch.int32)
-            rc = lib.fmoe_forward_routed_count(ctypes.byref(prob), topk_idx.data_ptr(),
-                                               topk_w.data_ptr(), num_tokens_dev.data_ptr(),
-                                               ctypes.byref(tens), ws.data_ptr(), ws.numel(),
-                                               stream)
+            if return_to is not None:
+                peers, src_start, row_shift, cap_rows, err = return_to
+                rc = lib.fmoe_forward_routed_count_p2p(
+                    ctypes.byref(prob), topk_idx.data_ptr(), topk_w.data_ptr(),
+                    num_tokens_dev.data_ptr(), ctypes.byref(tens), ws.data_ptr(), ws.numel(),
+                    peers.back_ptrs.data_ptr(), src_start.data_ptr(), row_shift.data_ptr(),
+                    row_shift.shape[0], cap_rows, err.data_ptr(), stream)
+            else:
+                rc = lib.fmoe_forward_routed_count(ctypes.byref(prob), topk_idx.data_ptr(),
+                                                   topk_w.data_ptr(), num_tokens_dev.data_ptr(),
+                                                   ctypes.byref(tens), ws.data_ptr(),
+                                                   ws.numel(), stream)
         else:
             fwd = lib.fmoe_forward_routed_prelaid if prelaid else lib.fmoe_forward_routed
             rc = fwd(ctypes.byref(prob), topk_idx.data_ptr(), topk_w.data_ptr(),

@@ -212,7 +212,7 @@ class ExpertParallelMoE:
                                self.rsf, num_local_experts=self.e_per_rank,
                                local_expert_offset=self.local_offset)
 
-    def _local_gpu(self, idx, w, hs, sc, offset, count=None, out=None):
+    def _local_gpu(self, idx, w, hs, sc, offset, count=None, out=None, return_to=None):
         import fmoe_b200
 
         ws = self.weights
@@ -220,7 +220,7 @@ class ExpertParallelMoE:
                                         ws["gemm1_weights_scale"], ws["gemm2_weights"],
                                         ws["gemm2_weights_scale"], offset, self.num_experts,
                                         n_group=self.n_group, topk_group=self.topk_group,
-                                        num_tokens_dev=count, out=out)
+                                        num_tokens_dev=count, out=out, return_to=return_to)
 
     # ---- peer-memory exchange -----------------------------------------------------------
     def _barrier(self):
@@ -311,7 +311,9 @@ class ExpertParallelMoE:
         max_tokens per rank; the per-destination counts are all-gathered on the device, the
         row offsets and the received row count computed there (fmoe_ep_offsets), and the
         unpack and the local operator take that count from device memory, so the host only
-        enqueues work and the local operator replays one cached graph."""
+        enqueues work and the local operator replays one cached graph. The operator's
+        combine writes the partial rows straight into the sources' return buffers
+        (fmoe_forward_routed_count_p2p), so no separate return pass runs."""
         import fmoe_b200
 
         T, H = hidden_states.shape
@@ -347,14 +349,15 @@ class ExpertParallelMoE:
         hs_r, sc_r, idx_r, w_r = fmoe_b200.ep_unpack_count(self._peers.recv[me], cap, rows, H, K,
                                                            out=st["unpacked"], device=dev)
         mark()
-        part = self._local(idx_r, w_r, hs_r, sc_r, count=rows, out=st["part"])
+        # the operator's combine stores each partial row straight into its source's buffer
+        self._local(idx_r, w_r, hs_r, sc_r, count=rows, out=st["part"],
+                    return_to=(self._peers, tables[world:2 * world + 1],
+                               tables[2 * world + 1:], cap, self._err))
         mark()
-        fmoe_b200.ep_return_p2p(part, tables[world:2 * world + 1], self._peers,
-                                tables[2 * world + 1:], cap, self._err)
         self._barrier()
         return fmoe_b200.ep_combine(self._peers.back[me], pos, T, H)
 
-    def _local(self, idx_r, w_r, hs_r, sc_r, count=None, out=None):
+    def _local(self, idx_r, w_r, hs_r, sc_r, count=None, out=None, return_to=None):
         """The rank's own experts on what it received (`count`: device token count, the
         tensors then sized for a capacity). In a timed pass on CUDA with the default
         kernels, also records the operator's stage times (route, permute, gemm1, gemm2,
@@ -363,7 +366,7 @@ class ExpertParallelMoE:
             if self.local_fn != self._local_gpu:
                 raise ValueError("a device-side token count needs the default local operator")
             run = lambda: self._local_gpu(idx_r, w_r, hs_r, sc_r, self.local_offset,  # noqa
-                                          count=count, out=out)
+                                          count=count, out=out, return_to=return_to)
         else:
             run = lambda: self.local_fn(idx_r, w_r, hs_r, sc_r, self.local_offset)  # noqa
         if not (self._timed and hs_r.device.type == "cuda" and self.local_fn == self._local_gpu):

@@ -127,6 +127,20 @@ int fmoe_forward_routed_count(const fmoe_problem* p, const int32_t* topk_idx,
                               const float* topk_w, const int32_t* num_tokens_dev,
                               const fmoe_tensors* t, void* workspace, size_t workspace_bytes,
                               void* stream);
+/* fmoe_forward_routed_count whose combine writes each output row straight back to the rank
+ * its token came from (expert-parallel return over peer memory, replacing fmoe_ep_return_p2p
+ * after the operator): row r, from the source s with src_start[s] <= r < src_start[s + 1],
+ * goes to peer_out[s] at row r + row_shift[s] (peer_out: device array of `world` buffer
+ * addresses; src_start / row_shift as for fmoe_ep_return_p2p). Rows outside
+ * [0, capacity_rows) are not written and set bit 1 of *err. t->output must still be a valid
+ * 16-byte aligned pointer; it is not written. The caller orders the ranks with a barrier
+ * after the call, as after fmoe_ep_return_p2p. */
+int fmoe_forward_routed_count_p2p(const fmoe_problem* p, const int32_t* topk_idx,
+                                  const float* topk_w, const int32_t* num_tokens_dev,
+                                  const fmoe_tensors* t, void* workspace, size_t workspace_bytes,
+                                  void* const* peer_out, const int64_t* src_start,
+                                  const int64_t* row_shift, int world, int64_t capacity_rows,
+                                  int* err, void* stream);
 
 /* Weight pre-layout (the weight side of the reference's per-call dequantise passes,
  * kernel.cu:924-1003, done once instead): writes every 32 KB weight tile the GEMMs load per

@@ -214,6 +214,57 @@ def test_count_entry_points_match_exact_sizes():
     assert fmoe_b200.poll_device_error() == 0
 
 
+def test_operator_returns_rows_straight_to_sources():
+    """fmoe_forward_routed_count_p2p: the combine writes row r of source s at row
+    r + row_shift[s] of buffer s (here two local buffers stand in for two ranks' return
+    buffers), bit-identical to the rows of the plain call; rows past the count and the
+    rows of `out` are not written; a shift out of the capacity is flagged, not written."""
+    import types
+    import fmoe_b200
+    from fmoe_b200 import workloads as W
+
+    H, K, R, cap, EL = 7168, 8, 150, 256, 32
+    geo = W.DSV3
+    acts = W.make_activations(geo, R, 8, device="cuda")
+    idx, w = fmoe_b200.route(acts["routing_logits"], acts["routing_bias"], 8, 4, 8, 2.5)
+    wts = W.make_expert_slice(geo, 2, 0, EL, device="cuda")
+    wl = [wts[k] for k in W.OPERATOR_ARGS[4:]]
+    hs = torch.zeros(cap, H, dtype=torch.float8_e4m3fn, device="cuda")
+    sc = torch.ones(H // 128, cap, dtype=torch.float32, device="cuda")
+    ii = torch.full((cap, K), 1, dtype=torch.int32, device="cuda")
+    ww = torch.zeros(cap, K, dtype=torch.float32, device="cuda")
+    hs[:R] = acts["hidden_states"]
+    sc[:, :R] = acts["hidden_states_scale"]
+    ii[:R] = idx
+    ww[:R] = w
+    rows = torch.tensor([R], dtype=torch.int32, device="cuda")
+    plain = fmoe_b200.forward_routed(ii, ww, hs, sc, *wl, 0, 256, num_tokens_dev=rows)
+    bufs = [torch.full((cap, H), 3.0, dtype=torch.bfloat16, device="cuda") for _ in range(2)]
+    peers = types.SimpleNamespace(back_ptrs=torch.tensor([b.data_ptr() for b in bufs],
+                                                         dtype=torch.int64, device="cuda"))
+    src_start = torch.tensor([0, 60, R], dtype=torch.int64, device="cuda")
+    shift = torch.tensor([10, -60 + 7], dtype=torch.int64, device="cuda")
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    out = torch.full((cap, H), 5.0, dtype=torch.bfloat16, device="cuda")
+    for _ in range(3):  # eager, captured, replayed
+        for b in bufs:
+            b.fill_(3.0)
+        fmoe_b200.forward_routed(ii, ww, hs, sc, *wl, 0, 256, num_tokens_dev=rows, out=out,
+                                 return_to=(peers, src_start, shift, cap, err))
+        torch.cuda.synchronize()
+        assert torch.equal(bufs[0][10:70], plain[:60]) and torch.equal(bufs[1][7:97], plain[60:R])
+        assert bool((bufs[0][:10] == 3.0).all()) and bool((bufs[0][70:] == 3.0).all())
+        assert bool((bufs[1][:7] == 3.0).all()) and bool((bufs[1][97:] == 3.0).all())
+        assert bool((out == 5.0).all()) and err.item() == 0
+    shift[1] = cap  # every row of source 1 lands past the capacity
+    bufs[1].fill_(3.0)
+    fmoe_b200.forward_routed(ii, ww, hs, sc, *wl, 0, 256, num_tokens_dev=rows, out=out,
+                             return_to=(peers, src_start, shift, cap, err))
+    torch.cuda.synchronize()
+    assert err.item() == 2 and bool((bufs[1] == 3.0).all())
+    assert fmoe_b200.poll_device_error() == 0
+
+
 def test_exchange_entry_points_reject_bad_arguments():
     import fmoe_b200
 
