@@ -533,7 +533,8 @@ def run_ep(args, world, rank, local, peaks):
                                                                           (rank + 1) * per)
     weights = W.make_expert_set(W.DSV3, args.seed, mine, device="cuda")
     layer = ep.ExpertParallelMoE(weights=weights, exchange=args.exchange, placement=placement,
-                                 max_tokens=None if args.ep_host_sync else T)
+                                 max_tokens=None if args.ep_host_sync else T,
+                                 fused_return=not args.ep_separate_return)
     a4 = [acts[k] for k in W.OPERATOR_ARGS[:4]]
     for _ in range(args.warmup):
         layer.forward(*a4)
@@ -846,6 +847,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--placement", choices=("balanced", "contiguous"), default="balanced",
                     help="N>1: expert placement over the ranks")
+    ap.add_argument("--ep-separate-return", action="store_true",
+                    help="N>1: return the partial rows with a separate kernel after the "
+                         "operator instead of from the operator's combine")
     ap.add_argument("--ep-host-sync", action="store_true",
                     help="N>1: size each step's exchange on the host (one device-to-host read "
                          "of the counts per step) instead of the sync-free device offsets")

@@ -298,7 +298,12 @@ __global__ void __launch_bounds__(128) combine_kernel(CombineArgs a) {
     for (int j = 0; j < 4; ++j) oh[j] = __floats2bfloat162_rn(acc[u][2 * j], acc[u][2 * j + 1]);
     *reinterpret_cast<uint4*>(dst + v * 8) = o;
   }
-  if (a.peer_out) __threadfence_system();  // the rows are read by the peer after a barrier
+  if (a.peer_out) {
+    // the rows are read by the peer after a barrier: one system-scope fence per CTA, after
+    // the CTA barrier (cumulative over every thread's stores)
+    __syncthreads();
+    if (threadIdx.x == 0) __threadfence_system();
+  }
 }
 
 template __global__ void combine_kernel<1>(CombineArgs a);

@@ -139,7 +139,8 @@ class ExpertParallelMoE:
                  top_k: int = 8, routed_scaling_factor: float = 2.5, group=None,
                  weights: Optional[dict] = None, route_fn: Optional[RouteFn] = None,
                  local_fn: Optional[LocalFn] = None, fused_exchange: bool = True,
-                 exchange: str = "p2p", placement=None, max_tokens: Optional[int] = None):
+                 exchange: str = "p2p", placement=None, max_tokens: Optional[int] = None,
+                 fused_return: bool = True):
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
@@ -173,6 +174,7 @@ class ExpertParallelMoE:
         if max_tokens is not None and max_tokens <= 0:
             raise ValueError("max_tokens must be positive")
         self.max_tokens = max_tokens
+        self.fused_return = fused_return
         self._static = None      # device-side offset state of the host-sync-free P2P step
         self._peers = None       # fmoe_b200.PeerBuffers, sized for _cap_tokens per rank
         self._cap_tokens = 0
@@ -349,11 +351,17 @@ class ExpertParallelMoE:
         hs_r, sc_r, idx_r, w_r = fmoe_b200.ep_unpack_count(self._peers.recv[me], cap, rows, H, K,
                                                            out=st["unpacked"], device=dev)
         mark()
-        # the operator's combine stores each partial row straight into its source's buffer
-        self._local(idx_r, w_r, hs_r, sc_r, count=rows, out=st["part"],
-                    return_to=(self._peers, tables[world:2 * world + 1],
-                               tables[2 * world + 1:], cap, self._err))
-        mark()
+        if self.fused_return:
+            # the operator's combine stores each partial row straight into its source's buffer
+            self._local(idx_r, w_r, hs_r, sc_r, count=rows, out=st["part"],
+                        return_to=(self._peers, tables[world:2 * world + 1],
+                                   tables[2 * world + 1:], cap, self._err))
+            mark()
+        else:
+            part = self._local(idx_r, w_r, hs_r, sc_r, count=rows, out=st["part"])
+            mark()
+            fmoe_b200.ep_return_p2p(part, tables[world:2 * world + 1], self._peers,
+                                    tables[2 * world + 1:], cap, self._err)
         self._barrier()
         return fmoe_b200.ep_combine(self._peers.back[me], pos, T, H)
 
