@@ -3,7 +3,9 @@
 Each rank owns 256 / N consecutive experts. The EP layer's output for a rank's tokens is
 compared with the single-GPU operator run on the same tokens with all 256 experts local
 (E_local = 256), and the 256-expert single-GPU call is itself checked against the sum of
-its eight 32-expert slices (each slice is checked against the CPU oracle elsewhere).
+its eight 32-expert slices (each slice is checked against the CPU oracle elsewhere). The
+step without a host round trip (`max_tokens`) runs with a shuffled expert placement, its
+return from the operator's combine bit-identical to the separate return kernel.
 """
 import datetime
 import os
@@ -66,6 +68,21 @@ def _worker(rank, world, port, T, q):
     via_nccl = ep.ExpertParallelMoE(weights=local, exchange="nccl").forward(*a4)
     layer.close()
     same_rows = bool(torch.equal(out, via_nccl)) and bool(torch.equal(out, again))
+    # the step without a host round trip (device offsets and counts), with a shuffled expert
+    # placement; the return from the operator's combine against the separate return kernel
+    pl = torch.randperm(256, generator=torch.Generator().manual_seed(11)).tolist()
+    mine = pl[rank * per:(rank + 1) * per]
+    placed_w = {k: v[mine].contiguous() for k, v in full.items()}
+    outs = []
+    for fused_return in (True, False):
+        lay = ep.ExpertParallelMoE(weights=placed_w, placement=pl, max_tokens=T,
+                                   fused_return=fused_return)
+        outs.append(lay.forward(*a4))
+        outs.append(lay.forward(*a4))  # the second step replays the operator's graph
+        p2p_err |= lay.exchange_error()
+        lay.close()
+    same_rows = same_rows and all(torch.equal(outs[0], o) for o in outs[1:])
+    placed = outs[0]
     args = [acts[k] for k in W.OPERATOR_ARGS[:4]] + [full[k] for k in W.OPERATOR_ARGS[4:]]
     ref = fmoe_b200.kernel(*args, 0, 2.5)
     slices = torch.zeros(T, geo.hidden, dtype=torch.float32, device="cuda")
@@ -74,7 +91,8 @@ def _worker(rank, world, port, T, q):
         a = [acts[k] for k in W.OPERATOR_ARGS[:4]] + [sl[k] for k in W.OPERATOR_ARGS[4:]]
         slices += fmoe_b200.kernel(*a, 32 * s, 2.5).float()
     torch.cuda.synchronize()
-    q.put((rank, _close(out, ref), _close(ref, slices), same_rows, p2p_err))
+    q.put((rank, _close(out, ref), _close(ref, slices), same_rows, p2p_err,
+           _close(placed, ref)))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -91,8 +109,11 @@ def test_ep_two_gpus_matches_full_layer():
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    for rank, (ok_ep, rel_ep), (ok_sl, rel_sl), same_rows, p2p_err in res:
+    for rank, (ok_ep, rel_ep), (ok_sl, rel_sl), same_rows, p2p_err, (ok_pl, rel_pl) in res:
         assert ok_ep and rel_ep < 1e-2, (rank, rel_ep)
+        assert ok_pl and rel_pl < 1e-2, (rank, rel_pl)  # sync-free step, shuffled placement
         assert ok_sl and rel_sl < 1e-2, (rank, rel_sl)
-        assert same_rows, rank  # peer-memory and NCCL exchanges give identical outputs
+        # peer-memory and NCCL exchanges give identical outputs; so do the two returns of
+        # the sync-free step, and its repeated steps
+        assert same_rows, rank
         assert p2p_err == 0, (rank, p2p_err)
