@@ -190,10 +190,14 @@ def layer_config(T: int, world: int, exchange: str, placement: str = "balanced",
                 "row offsets and received-row counts computed on the device (no host round "
                 "trip per step)") if exchange == "p2p" else
             "NCCL all-to-all-v dispatch + combine, counts all-to-all")
-        cfg["placement"] = (
-            "balanced: experts assigned to ranks by longest-processing-time greedy on their "
-            "128-row tile counts in a calibration batch (other tokens, same layer)"
-            if placement == "balanced" else "contiguous 256/N-expert slices")
+        cfg["placement"] = {
+            "balanced": "balanced: experts assigned to ranks by longest-processing-time greedy "
+                        "on their 128-row tile counts in a calibration batch (other tokens, "
+                        "same layer)",
+            "local": "local: contiguous slices refined by expert swaps that lower the largest "
+                     "rank cost (128-row tiles + received tokens) on a calibration batch "
+                     "(other tokens, same layer)",
+        }.get(placement, "contiguous 256/N-expert slices")
     return cfg
 
 
@@ -522,12 +526,12 @@ def run_ep(args, world, rank, local, peaks):
     per = 256 // world
     acts = layer_activations(args.seed, rank, T)
     placement = None
-    if args.placement == "balanced":
+    if args.placement != "contiguous":
         # expert loads of a calibration batch: other tokens (seed offset), the same layer
         cal = W.make_activations(W.DSV3, T, args.seed + CAL_SEED + 1009 * rank, device="cuda")
         placement = ep.calibrate_placement(
             lambda lg, b: fmoe_b200.route(lg, b, 8, 4, 8, RSF), cal["routing_logits"],
-            acts["routing_bias"], 256)
+            acts["routing_bias"], 256, mode=args.placement)
         del cal
     mine = placement[rank * per:(rank + 1) * per] if placement else range(rank * per,
                                                                           (rank + 1) * per)
@@ -845,8 +849,8 @@ def main():
                          "(config 4: 8); 0 = grouped top-k over random logits")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--placement", choices=("balanced", "contiguous"), default="balanced",
-                    help="N>1: expert placement over the ranks")
+    ap.add_argument("--placement", choices=("local", "balanced", "contiguous"),
+                    default="balanced", help="N>1: expert placement over the ranks")
     ap.add_argument("--ep-separate-return", action="store_true",
                     help="N>1: return the partial rows with a separate kernel after the "
                          "operator instead of from the operator's combine")

@@ -109,18 +109,104 @@ def balanced_placement(rows, world: int) -> list:
     return [e for r in range(world) for e in sorted(owned[r])]
 
 
+# Relative cost of one token a rank receives, in 128-row GEMM tiles: a received token moves
+# 7,456 B in and 14,336 B back over NVLink (≈ 0.031 ms per thousand at ≈ 700 GB/s), a tile
+# of the 256-expert layer's GEMM1 + GEMM2 takes ≈ 4.25 µs on a B200 at ≈ 1,000 rows per
+# expert (8-GPU expert parallelism).
+RECV_TOKEN_COST_IN_TILES = 0.0073
+
+
+def locality_placement(topk_idx, num_experts: int, world: int, max_swaps: int = 256,
+                       recv_cost: float = RECV_TOKEN_COST_IN_TILES) -> list:
+    """An expert placement that evens out the ranks' work while keeping each token's experts
+    on few ranks: start from the contiguous slices (a DS-V3 routing group per rank at 8
+    ranks, so a token goes to at most topk_group ranks) and swap one expert of the most
+    loaded rank with one of another rank while that lowers the largest rank cost,
+    cost(r) = tiles(r) + recv_cost * tokens_received(r), with tiles counted as 128-row
+    token tiles of each expert's routed rows and tokens_received the tokens of `topk_idx`
+    ([T, K] expert ids of a calibration batch, all ranks' tokens) that need rank r. Each
+    step takes the best swap over all candidate pairs (deterministic). Returns the expert
+    ids in rank-major order."""
+    import numpy as np
+
+    idx = torch.as_tensor(topk_idx).to(torch.int64).cpu().numpy()
+    E = num_experts
+    if E % world:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    per = E // world
+    owner = np.arange(E) // per
+    if world == 1 or idx.size == 0:
+        return list(range(E))
+    T = idx.shape[0]
+    valid = (idx >= 0) & (idx < E)
+    rows = np.bincount(idx[valid], minlength=E)
+    tiles = (rows + 127) // 128
+    X = np.zeros((E, T), dtype=bool)  # expert e is selected by token t
+    for k in range(idx.shape[1]):
+        m = valid[:, k]
+        X[idx[m, k], np.nonzero(m)[0]] = True
+    Xb = np.packbits(X, axis=1)
+    C = np.zeros((world, T), dtype=np.int32)  # experts of token t on rank r
+    for e in range(E):
+        C[owner[e]] += X[e]
+    load = np.array([tiles[owner == r].sum() for r in range(world)], dtype=np.float64)
+    J = load + recv_cost * (C > 0).sum(1)
+    for _ in range(max_swaps):
+        a = int(np.argmax(J))
+        rest = np.delete(J, a)
+        ea = np.nonzero(owner == a)[0]
+        s2a, s1a = np.packbits(C[a] >= 2), np.packbits(C[a] == 1)
+        base_a = s2a[None, :] | (s1a[None, :] & ~Xb[ea])  # a without e, per e
+        best = None
+        for b in range(world):
+            if b == a:
+                continue
+            fb = np.nonzero(owner == b)[0]
+            s2b, s1b = np.packbits(C[b] >= 2), np.packbits(C[b] == 1)
+            base_b = s2b[None, :] | (s1b[None, :] & ~Xb[fb])  # b without f, per f
+            recv_a = np.bitwise_count(base_a[:, None, :] | Xb[fb][None, :, :]).sum(-1)
+            recv_b = np.bitwise_count(base_b[None, :, :] | Xb[ea][:, None, :]).sum(-1)
+            ja = load[a] - tiles[ea][:, None] + tiles[fb][None, :] + recv_cost * recv_a
+            jb = load[b] + tiles[ea][:, None] - tiles[fb][None, :] + recv_cost * recv_b
+            others = np.delete(rest, b - (b > a)).max() if world > 2 else -np.inf
+            jn = np.maximum(np.maximum(ja, jb), others)
+            i, j = np.unravel_index(int(np.argmin(jn)), jn.shape)
+            if best is None or jn[i, j] < best[0]:
+                best = (float(jn[i, j]), int(ea[i]), int(fb[j]), b)
+        if best is None or best[0] >= J.max() - 1e-9:
+            break
+        _, e, f, b = best
+        owner[e], owner[f] = b, a
+        C[a] += X[f].astype(np.int32) - X[e]
+        C[b] += X[e].astype(np.int32) - X[f]
+        load[a] += tiles[f] - tiles[e]
+        load[b] += tiles[e] - tiles[f]
+        J = load + recv_cost * (C > 0).sum(1)
+    return [int(e) for r in range(world) for e in np.nonzero(owner == r)[0]]
+
+
 def calibrate_placement(route_fn: RouteFn, routing_logits, routing_bias, num_experts: int,
-                        group=None) -> list:
-    """Route a calibration batch on every rank, add the per-expert row counts over the
-    ranks and return `balanced_placement` of the totals (the same list on every rank)."""
+                        group=None, mode: str = "balanced") -> list:
+    """Route a calibration batch on every rank and return a placement computed from it, the
+    same list on every rank: `balanced_placement` of the per-expert row counts added over
+    the ranks (mode "balanced"), or `locality_placement` of every rank's routing (mode
+    "local", the [T, K] ids all-gathered)."""
     idx, _ = route_fn(routing_logits, routing_bias)
-    idx = idx.reshape(-1).long()
-    rows = torch.bincount(idx[idx >= 0], minlength=num_experts).to(torch.int64)
-    if dist.is_initialized() and dist.get_world_size(group) > 1:
+    dist_on = dist.is_initialized() and dist.get_world_size(group) > 1
+    world = dist.get_world_size(group) if dist_on else 1
+    if mode == "local":
+        ids = idx.to(torch.int32).contiguous()
+        if dist_on:
+            parts = [None] * world
+            dist.all_gather_object(parts, ids.cpu(), group=group)
+            ids = torch.cat(parts)
+        return locality_placement(ids, num_experts, world)
+    if mode != "balanced":
+        raise ValueError(f"unknown placement mode {mode!r}")
+    flat = idx.reshape(-1).long()
+    rows = torch.bincount(flat[flat >= 0], minlength=num_experts).to(torch.int64)
+    if dist_on:
         dist.all_reduce(rows, group=group)
-        world = dist.get_world_size(group)
-    else:
-        world = 1
     return balanced_placement(rows, world)
 
 

@@ -67,10 +67,11 @@ def _ep_worker(rank, world, port, T, result_q, placement_mode=None):
     placement = None
     if placement_mode == "shuffle":
         placement = torch.randperm(GEO_E, generator=torch.Generator().manual_seed(5)).tolist()
-    elif placement_mode == "calibrated":
+    elif placement_mode in ("calibrated", "local"):
         cal = W.make_activations(geo, 64, seed=700 + rank, device="cpu")
         placement = ep.calibrate_placement(route_fn, cal["routing_logits"], acts["routing_bias"],
-                                           GEO_E)
+                                           GEO_E, mode="local" if placement_mode == "local"
+                                           else "balanced")
         allp = [None] * world
         dist.all_gather_object(allp, placement)
         assert all(p == placement for p in allp)
@@ -98,7 +99,7 @@ def _ep_worker(rank, world, port, T, result_q, placement_mode=None):
 
 
 @pytest.mark.parametrize("world,placement_mode", [(2, None), (4, None), (2, "shuffle"),
-                                                  (4, "calibrated")])
+                                                  (4, "calibrated"), (4, "local")])
 def test_ep_matches_full_layer(world, placement_mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -134,6 +135,52 @@ def test_balanced_placement():
         assert pl == ep.balanced_placement(rows.tolist(), world)  # deterministic
     with pytest.raises(ValueError):
         ep.balanced_placement(rows[:255], 2)
+
+
+def _skewed_routing(T, E, K, seed):
+    g = torch.Generator().manual_seed(seed)
+    pop = torch.rand(E, generator=g) ** 3 + 0.02  # skewed expert popularity
+    idx = torch.stack([torch.multinomial(pop, K, replacement=False, generator=g)
+                       for _ in range(T)]).to(torch.int32)
+    idx[torch.rand(T, K, generator=g) < 0.02] = -1  # a few unselected slots
+    return idx
+
+
+def _rank_costs(idx, placement, world, recv_cost):
+    import numpy as np
+
+    E = len(placement)
+    per = E // world
+    owner = np.zeros(E, dtype=np.int64)
+    for i, e in enumerate(placement):
+        owner[e] = i // per
+    ids = idx.numpy()
+    valid = ids >= 0
+    rows = np.bincount(ids[valid], minlength=E)
+    tiles = np.array([((rows[owner == r] + 127) // 128).sum() for r in range(world)])
+    recv = np.zeros(world)
+    for t in range(ids.shape[0]):
+        for r in set(owner[ids[t][valid[t]]].tolist()):
+            recv[r] += 1
+    return tiles + recv_cost * recv
+
+
+def test_locality_placement():
+    from fmoe_b200 import ep
+
+    E, K = 64, 4
+    idx = _skewed_routing(1500, E, K, seed=7)
+    assert ep.locality_placement(idx, E, 1) == list(range(E))
+    for world in (2, 4, 8):
+        pl = ep.locality_placement(idx, E, world)
+        assert sorted(pl) == list(range(E))
+        assert pl == ep.locality_placement(idx.clone(), E, world)  # deterministic
+        rc = ep.RECV_TOKEN_COST_IN_TILES
+        local = _rank_costs(idx, pl, world, rc)
+        contig = _rank_costs(idx, list(range(E)), world, rc)
+        assert local.max() <= contig.max() + 1e-9
+    with pytest.raises(ValueError):
+        ep.locality_placement(idx, 63, 2)
 
 
 def test_placement_validation():
