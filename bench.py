@@ -20,9 +20,10 @@ tokens; the step time is the max over ranks (CUDA events), `value` counts all ra
              the bound is whichever roofline time is longer
   ep_parity  32 tokens per rank of the step's output against the single-GPU operator run
              on each rank's experts (local_expert_offset) and summed in rank order
-  placement  (N>1) which experts each rank owns: balanced by default (greedy on the
-             128-row tile counts of a calibration batch of other tokens), or contiguous
-             256/N slices with --placement contiguous
+  placement  (N>1) which experts each rank owns, from a calibration batch of other
+             tokens: by default the contiguous slices refined by cost-lowering expert swaps
+             (--placement local); --placement balanced (greedy on 128-row tile counts) or
+             contiguous (the reference's 256/N slices) for comparison
   cpu_baseline  (N=1) the CPU oracle (PyTorch fp32 dequantise reference) on this host's
              cores, a bounded sample: 64 tokens of the same layer
   sweep      (N=1) BASELINE configs 1, 2 and 4 on one 32-expert slice (T = 1..8192 and the
@@ -174,7 +175,7 @@ def layer_weights(seed: int, first: int, count: int, device="cuda"):
     return W.make_expert_slice(W.DSV3, seed, first, count, device=device)
 
 
-def layer_config(T: int, world: int, exchange: str, placement: str = "balanced",
+def layer_config(T: int, world: int, exchange: str, placement: str = "local",
                  host_sync: bool = False) -> dict:
     per = 256 // world
     cfg = {"workload": "config3_dsv3_full_layer", "tokens_per_rank": T, "hidden": H,
@@ -850,7 +851,7 @@ def main():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--placement", choices=("local", "balanced", "contiguous"),
-                    default="balanced", help="N>1: expert placement over the ranks")
+                    default="local", help="N>1: expert placement over the ranks")
     ap.add_argument("--ep-separate-return", action="store_true",
                     help="N>1: return the partial rows with a separate kernel after the "
                          "operator instead of from the operator's combine")
