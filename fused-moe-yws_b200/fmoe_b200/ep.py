@@ -296,9 +296,10 @@ class ExpertParallelMoE:
     def _route_gpu(self, logits, bias):
         import fmoe_b200
 
+        # only the (id, weight) pairs are used here: the routing kernel's local plan is kept
+        # to one expert (the receiving ranks plan their own experts)
         return fmoe_b200.route(logits, bias, self.n_group, self.topk_group, self.top_k,
-                               self.rsf, num_local_experts=self.e_per_rank,
-                               local_expert_offset=self.local_offset)
+                               self.rsf, num_local_experts=1, local_expert_offset=0)
 
     def _local_gpu(self, idx, w, hs, sc, offset, count=None, out=None, return_to=None):
         import fmoe_b200
