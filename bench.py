@@ -532,7 +532,7 @@ def run_ep(args, world, rank, local, peaks):
         cal = W.make_activations(W.DSV3, T, args.seed + CAL_SEED + 1009 * rank, device="cuda")
         placement = ep.calibrate_placement(
             lambda lg, b: fmoe_b200.route(lg, b, 8, 4, 8, RSF), cal["routing_logits"],
-            acts["routing_bias"], 256, mode=args.placement)
+            acts["routing_bias"], 256, mode=args.placement, search=args.placement_search)
         del cal
     mine = placement[rank * per:(rank + 1) * per] if placement else range(rank * per,
                                                                           (rank + 1) * per)
@@ -852,6 +852,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--placement", choices=("local", "balanced", "contiguous"),
                     default="local", help="N>1: expert placement over the ranks")
+    ap.add_argument("--placement-search", choices=("pairs", "max-rank"), default="pairs",
+                    help="N>1, --placement local: swap search of the locality placement")
     ap.add_argument("--ep-separate-return", action="store_true",
                     help="N>1: return the partial rows with a separate kernel after the "
                          "operator instead of from the operator's combine")

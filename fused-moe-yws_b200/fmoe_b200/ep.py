@@ -117,22 +117,28 @@ RECV_TOKEN_COST_IN_TILES = 0.0073
 
 
 def locality_placement(topk_idx, num_experts: int, world: int, max_swaps: int = 256,
-                       recv_cost: float = RECV_TOKEN_COST_IN_TILES) -> list:
+                       recv_cost: float = RECV_TOKEN_COST_IN_TILES, search: str = "pairs",
+                       power: float = 16.0) -> list:
     """An expert placement that evens out the ranks' work while keeping each token's experts
-    on few ranks: start from the contiguous slices (a DS-V3 routing group per rank at 8
-    ranks, so a token goes to at most topk_group ranks) and swap one expert of the most
-    loaded rank with one of another rank while that lowers the largest rank cost,
-    cost(r) = tiles(r) + recv_cost * tokens_received(r), with tiles counted as 128-row
+    on few ranks. Starts from the contiguous slices (a DS-V3 routing group per rank at 8
+    ranks, so a token goes to at most topk_group ranks) and swaps experts between ranks.
+    Rank cost: cost(r) = tiles(r) + recv_cost * tokens_received(r), tiles counted as 128-row
     token tiles of each expert's routed rows and tokens_received the tokens of `topk_idx`
-    ([T, K] expert ids of a calibration batch, all ranks' tokens) that need rank r. Each
-    step takes the best swap over all candidate pairs (deterministic). Returns the expert
-    ids in rank-major order."""
+    ([T, K] expert ids of a calibration batch, all ranks' tokens) that need rank r.
+    search "pairs": each step takes the swap, over every pair of ranks, that lowers
+    sum_r (cost(r) / mean cost) ** power the most (a smooth stand-in for the largest cost,
+    which lets several ranks improve at once), and the placement with the lowest largest
+    cost seen is returned. search "max-rank": each step takes the swap of an expert of the
+    most loaded rank that lowers the largest cost the most. Deterministic; returns the
+    expert ids in rank-major order."""
     import numpy as np
 
     idx = torch.as_tensor(topk_idx).to(torch.int64).cpu().numpy()
     E = num_experts
     if E % world:
         raise ValueError(f"{E} experts do not split over {world} ranks")
+    if search not in ("pairs", "max-rank"):
+        raise ValueError(f"unknown search {search!r}")
     per = E // world
     owner = np.arange(E) // per
     if world == 1 or idx.size == 0:
@@ -151,42 +157,61 @@ def locality_placement(topk_idx, num_experts: int, world: int, max_swaps: int = 
         C[owner[e]] += X[e]
     load = np.array([tiles[owner == r].sum() for r in range(world)], dtype=np.float64)
     J = load + recv_cost * (C > 0).sum(1)
+    scale = max(float(J.mean()), 1e-9)
+    best_owner, best_max = owner.copy(), float(J.max())
+
+    def swap_costs(a, b):
+        # costs of ranks a and b after swapping expert ea[i] (on a) with fb[j] (on b)
+        ea, fb = np.nonzero(owner == a)[0], np.nonzero(owner == b)[0]
+        base_a = np.packbits(C[a] >= 2)[None, :] | (np.packbits(C[a] == 1)[None, :] & ~Xb[ea])
+        base_b = np.packbits(C[b] >= 2)[None, :] | (np.packbits(C[b] == 1)[None, :] & ~Xb[fb])
+        recv_a = np.bitwise_count(base_a[:, None, :] | Xb[fb][None, :, :]).sum(-1)
+        recv_b = np.bitwise_count(base_b[None, :, :] | Xb[ea][:, None, :]).sum(-1)
+        ja = load[a] - tiles[ea][:, None] + tiles[fb][None, :] + recv_cost * recv_a
+        jb = load[b] + tiles[ea][:, None] - tiles[fb][None, :] + recv_cost * recv_b
+        return ea, fb, ja, jb
+
     for _ in range(max_swaps):
-        a = int(np.argmax(J))
-        rest = np.delete(J, a)
-        ea = np.nonzero(owner == a)[0]
-        s2a, s1a = np.packbits(C[a] >= 2), np.packbits(C[a] == 1)
-        base_a = s2a[None, :] | (s1a[None, :] & ~Xb[ea])  # a without e, per e
         best = None
-        for b in range(world):
-            if b == a:
-                continue
-            fb = np.nonzero(owner == b)[0]
-            s2b, s1b = np.packbits(C[b] >= 2), np.packbits(C[b] == 1)
-            base_b = s2b[None, :] | (s1b[None, :] & ~Xb[fb])  # b without f, per f
-            recv_a = np.bitwise_count(base_a[:, None, :] | Xb[fb][None, :, :]).sum(-1)
-            recv_b = np.bitwise_count(base_b[None, :, :] | Xb[ea][:, None, :]).sum(-1)
-            ja = load[a] - tiles[ea][:, None] + tiles[fb][None, :] + recv_cost * recv_a
-            jb = load[b] + tiles[ea][:, None] - tiles[fb][None, :] + recv_cost * recv_b
-            others = np.delete(rest, b - (b > a)).max() if world > 2 else -np.inf
-            jn = np.maximum(np.maximum(ja, jb), others)
-            i, j = np.unravel_index(int(np.argmin(jn)), jn.shape)
-            if best is None or jn[i, j] < best[0]:
-                best = (float(jn[i, j]), int(ea[i]), int(fb[j]), b)
-        if best is None or best[0] >= J.max() - 1e-9:
-            break
-        _, e, f, b = best
+        if search == "pairs":
+            for a in range(world):
+                for b in range(a + 1, world):
+                    ea, fb, ja, jb = swap_costs(a, b)
+                    delta = ((ja / scale) ** power + (jb / scale) ** power
+                             - (J[a] / scale) ** power - (J[b] / scale) ** power)
+                    i, j = np.unravel_index(int(np.argmin(delta)), delta.shape)
+                    if best is None or delta[i, j] < best[0]:
+                        best = (float(delta[i, j]), int(ea[i]), int(fb[j]), a, b)
+            if best is None or best[0] >= -1e-12:
+                break
+        else:
+            a = int(np.argmax(J))
+            rest = np.delete(J, a)
+            for b in range(world):
+                if b == a:
+                    continue
+                ea, fb, ja, jb = swap_costs(a, b)
+                others = np.delete(rest, b - (b > a)).max() if world > 2 else -np.inf
+                jn = np.maximum(np.maximum(ja, jb), others)
+                i, j = np.unravel_index(int(np.argmin(jn)), jn.shape)
+                if best is None or jn[i, j] < best[0]:
+                    best = (float(jn[i, j]), int(ea[i]), int(fb[j]), a, b)
+            if best is None or best[0] >= J.max() - 1e-9:
+                break
+        _, e, f, a, b = best
         owner[e], owner[f] = b, a
         C[a] += X[f].astype(np.int32) - X[e]
         C[b] += X[e].astype(np.int32) - X[f]
         load[a] += tiles[f] - tiles[e]
         load[b] += tiles[e] - tiles[f]
         J = load + recv_cost * (C > 0).sum(1)
-    return [int(e) for r in range(world) for e in np.nonzero(owner == r)[0]]
+        if J.max() < best_max - 1e-9:
+            best_owner, best_max = owner.copy(), float(J.max())
+    return [int(e) for r in range(world) for e in np.nonzero(best_owner == r)[0]]
 
 
 def calibrate_placement(route_fn: RouteFn, routing_logits, routing_bias, num_experts: int,
-                        group=None, mode: str = "balanced") -> list:
+                        group=None, mode: str = "balanced", search: str = "pairs") -> list:
     """Route a calibration batch on every rank and return a placement computed from it, the
     same list on every rank: `balanced_placement` of the per-expert row counts added over
     the ranks (mode "balanced"), or `locality_placement` of every rank's routing (mode
@@ -200,7 +225,7 @@ def calibrate_placement(route_fn: RouteFn, routing_logits, routing_bias, num_exp
             parts = [None] * world
             dist.all_gather_object(parts, ids.cpu(), group=group)
             ids = torch.cat(parts)
-        return locality_placement(ids, num_experts, world)
+        return locality_placement(ids, num_experts, world, search=search)
     if mode != "balanced":
         raise ValueError(f"unknown placement mode {mode!r}")
     flat = idx.reshape(-1).long()

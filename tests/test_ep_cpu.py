@@ -172,13 +172,14 @@ def test_locality_placement():
     idx = _skewed_routing(1500, E, K, seed=7)
     assert ep.locality_placement(idx, E, 1) == list(range(E))
     for world in (2, 4, 8):
-        pl = ep.locality_placement(idx, E, world)
-        assert sorted(pl) == list(range(E))
-        assert pl == ep.locality_placement(idx.clone(), E, world)  # deterministic
-        rc = ep.RECV_TOKEN_COST_IN_TILES
-        local = _rank_costs(idx, pl, world, rc)
-        contig = _rank_costs(idx, list(range(E)), world, rc)
-        assert local.max() <= contig.max() + 1e-9
+        for search in ("pairs", "max-rank"):
+            pl = ep.locality_placement(idx, E, world, search=search)
+            assert sorted(pl) == list(range(E))
+            assert pl == ep.locality_placement(idx.clone(), E, world, search=search)
+            rc = ep.RECV_TOKEN_COST_IN_TILES
+            local = _rank_costs(idx, pl, world, rc)
+            contig = _rank_costs(idx, list(range(E)), world, rc)
+            assert local.max() <= contig.max() + 1e-9
     with pytest.raises(ValueError):
         ep.locality_placement(idx, 63, 2)
 
