@@ -852,7 +852,7 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--placement", choices=("local", "balanced", "contiguous"),
                     default="local", help="N>1: expert placement over the ranks")
-    ap.add_argument("--placement-search", choices=("pairs", "max-rank"), default="pairs",
+    ap.add_argument("--placement-search", choices=("max-rank", "pairs"), default="max-rank",
                     help="N>1, --placement local: swap search of the locality placement")
     ap.add_argument("--ep-separate-return", action="store_true",
                     help="N>1: return the partial rows with a separate kernel after the "

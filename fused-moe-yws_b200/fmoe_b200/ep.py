@@ -117,7 +117,7 @@ RECV_TOKEN_COST_IN_TILES = 0.0073
 
 
 def locality_placement(topk_idx, num_experts: int, world: int, max_swaps: int = 256,
-                       recv_cost: float = RECV_TOKEN_COST_IN_TILES, search: str = "pairs",
+                       recv_cost: float = RECV_TOKEN_COST_IN_TILES, search: str = "max-rank",
                        power: float = 16.0) -> list:
     """An expert placement that evens out the ranks' work while keeping each token's experts
     on few ranks. Starts from the contiguous slices (a DS-V3 routing group per rank at 8
@@ -125,12 +125,13 @@ def locality_placement(topk_idx, num_experts: int, world: int, max_swaps: int = 
     Rank cost: cost(r) = tiles(r) + recv_cost * tokens_received(r), tiles counted as 128-row
     token tiles of each expert's routed rows and tokens_received the tokens of `topk_idx`
     ([T, K] expert ids of a calibration batch, all ranks' tokens) that need rank r.
-    search "pairs": each step takes the swap, over every pair of ranks, that lowers
-    sum_r (cost(r) / mean cost) ** power the most (a smooth stand-in for the largest cost,
-    which lets several ranks improve at once), and the placement with the lowest largest
-    cost seen is returned. search "max-rank": each step takes the swap of an expert of the
-    most loaded rank that lowers the largest cost the most. Deterministic; returns the
-    expert ids in rank-major order."""
+    search "max-rank" (default): each step takes the swap of an expert of the most loaded
+    rank that lowers the largest cost the most. search "pairs": each step takes the swap,
+    over every pair of ranks, that lowers sum_r (cost(r) / mean cost) ** power the most (a
+    smooth stand-in for the largest cost), and the placement with the lowest largest cost
+    seen is returned; it balances the model cost better (8 ranks: busiest 1.034x the mean
+    against 1.078x) but measured 1.2 % slower per step on 8 B200s (3.390 against 3.348 ms).
+    Deterministic; returns the expert ids in rank-major order."""
     import numpy as np
 
     idx = torch.as_tensor(topk_idx).to(torch.int64).cpu().numpy()
@@ -211,7 +212,7 @@ def locality_placement(topk_idx, num_experts: int, world: int, max_swaps: int = 
 
 
 def calibrate_placement(route_fn: RouteFn, routing_logits, routing_bias, num_experts: int,
-                        group=None, mode: str = "balanced", search: str = "pairs") -> list:
+                        group=None, mode: str = "balanced", search: str = "max-rank") -> list:
     """Route a calibration batch on every rank and return a placement computed from it, the
     same list on every rank: `balanced_placement` of the per-expert row counts added over
     the ranks (mode "balanced"), or `locality_placement` of every rank's routing (mode
