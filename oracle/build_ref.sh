@@ -13,8 +13,11 @@
 # from the flashinfer wheel (solution/cuda/kernel.cu includes cutlass/*), TVM-FFI headers
 # and libtvm_ffi.so from the tvm_ffi wheel.
 set -euo pipefail
-REF_SRC="${FMOE_REFERENCE_ROOT:-/root/reference}/solution/cuda/kernel.cu"
 HERE="$(cd "$(dirname "$0")" && pwd)"
+# the reference checkout: FMOE_REFERENCE_ROOT, else a `reference` directory beside this
+# repository's own directory
+REF_ROOT="${FMOE_REFERENCE_ROOT:-$(cd "$HERE/../.." && pwd)/reference}"
+REF_SRC="$REF_ROOT/solution/cuda/kernel.cu"
 OUT="$HERE/_ref"
 if [ ! -f "$REF_SRC" ]; then
   echo "reference source not found at $REF_SRC; skipping" >&2
