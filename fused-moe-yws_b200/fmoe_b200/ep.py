@@ -23,11 +23,17 @@ Expert placement: by default rank r owns the contiguous experts [r*E/N, (r+1)*E/
 reference's slice (`local_expert_offset = r*E/N`). Routing skew makes those slices unequal
 (with the DS-V3 config-3 workload the busiest of 8 slices has 1.3x the mean rows), and every
 step waits for the busiest rank. `placement` assigns any E/N experts to each rank instead
-(rank r owns placement[r*E/N : (r+1)*E/N], its weights stacked in that order);
-`balanced_placement` computes one from per-expert row counts, such as those of a
-calibration batch (`calibrate_placement`). Internally each routed expert id is replaced by
-its position in the placement, so the destination rank is position // (E/N) and the local
+(rank r owns placement[r*E/N : (r+1)*E/N], its weights stacked in that order).
+`locality_placement` computes one from a calibration batch's routing that evens out the
+ranks' work while keeping each token's experts on few ranks, `balanced_placement` one from
+per-expert row counts alone; `calibrate_placement` routes the batch on every rank and
+returns the same placement everywhere. Internally each routed expert id is replaced by its
+position in the placement, so the destination rank is position // (E/N) and the local
 operator runs with local_expert_offset = r*E/N, exactly as for the contiguous slices.
+
+Without a host round trip (`max_tokens`): buffers are sized once, the counts are gathered
+and the row offsets computed on the device, and the local operator reads the received token
+count from device memory and returns its rows straight to the sources from its combine.
 
 On CUDA the send plan, the payload packing and unpacking and the rank-ordered combine are
 kernels of the library (`fmoe_ep_*` in include/fmoe.h: one launch each, instead of chains
