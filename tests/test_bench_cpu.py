@@ -16,8 +16,23 @@ def test_help_lists_the_contract_options():
     # stdout is kept for the one JSON line, so everything else (help included) goes to stderr
     text = r.stdout + r.stderr
     for opt in ("--gpus", "--steps", "--warmup", "--impl", "--tokens", "--skew", "--exchange",
-                "--sweep-tiles", "--sweep-tokens", "--no-sweep", "--no-cpu"):
+                "--sweep-tiles", "--sweep-tokens", "--no-sweep", "--no-cpu", "--placement",
+                "--placement-search", "--ep-host-sync", "--ep-separate-return"):
         assert opt in text, opt
+
+
+def test_layer_config_names_the_workload_and_the_exchange():
+    import bench
+
+    one = bench.layer_config(4096, 1, "p2p")
+    assert one["workload"] == "config3_dsv3_full_layer" and one["experts_per_rank"] == 256
+    assert "collectives" not in one and "placement" not in one  # no exchange on one GPU
+    eight = bench.layer_config(4096, 8, "p2p")
+    assert eight["experts_per_rank"] == 32 and eight["parallelism"] == "ep8"
+    assert eight["placement"].startswith("local") and "no host round" in eight["collectives"]
+    assert bench.layer_config(4096, 8, "p2p", "contiguous")["placement"].startswith("contiguous")
+    assert "host each step" in bench.layer_config(4096, 2, "p2p", "local", True)["collectives"]
+    assert "all-to-all" in bench.layer_config(4096, 2, "nccl")["collectives"]
 
 
 def test_roofline_constants_match_the_dsv3_shapes():
